@@ -1,0 +1,441 @@
+#!/usr/bin/env python
+"""Benchmark: W4A8 GEMV weight-stream throughput on B200 (libkernelsmith).
+
+Workload (the W4A8 GEMV configuration of the headline metric):
+  W int4 [11008, 4096] packed low nibble first, group 32 along K with f16
+  scales, x int8 [4096] with per-token f32 scale 0.02, f32 output.
+  One step = 64 such GEMVs over 64 distinct resident weight matrices (the
+  gate and up projections of a 32-layer 7B-class model for one decode
+  token), each with its own activation vector: 1.63 GB of weights and
+  scales, far larger than the 126 MB L2, so no flush is needed.
+
+  N > 1 GPUs (weak scaling): each rank holds an 11008-row shard of each of
+  the 64 matrices ([N*11008, 4096] globally), runs the same per-GPU work as
+  N = 1, and the output slices are all-gathered over NVLink with NCCL in four
+  chunks of 16 GEMVs, each overlapped with the next chunk's GEMVs on a
+  second stream.
+
+Numbers:
+  value      algorithmic bytes of all GEMVs of all ranks / device time (TB/s),
+             weights already resident in HBM, CUDA events on the launching
+             stream, max over ranks.
+  e2e        same metric through the public synchronous C ABI
+             (ks_b200_matvec_w4a8_f16) with pinned HOST buffers: every GEMV
+             copies its weights, scales and x host->device and its output
+             back inside the timed region.
+  roofline   achieved GB/s of the GEMV kernel (bytes per launch / average
+             launch time over the timed region) against the measured HBM peak.
+  cpu_baseline  the reference's own C implementation (ks_matvec_w4a8 built
+             from the reference sources, f32 scales) on this host's cores,
+             rows split across threads.
+
+--impl reference runs only the reference CPU path on rank 0 and prints its
+line; other ranks exit without work.
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "ulir-kernels_b200", ROOT / "oracle"):
+    sys.path.insert(0, str(_p))
+
+METRIC = "INT8/W4A8 GEMV weight-stream TB/s & % HBM peak at 1/2/4/8 B200"
+ROWS, COLS, GROUP = 11008, 4096, 32
+SX = 0.02
+MATS = 64
+CHUNKS = 4
+SEED = 20261201
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the W4A8 kernel
+# on this workload, from the ncu capture summarised in
+# profiles/w4a8_gemv_11008x4096_g32.md (None until captured).
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def gemv_bytes(rows=ROWS, cols=COLS, group=GROUP, scale_bytes=2) -> int:
+    """Algorithmic bytes of one GEMV: packed weights + scales + x + y."""
+    return rows * (cols // 2) + rows * (cols // group) * scale_bytes + cols + rows * 4
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer e2e loop")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------ CPU baseline --
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def make_host_inputs(seed=SEED):
+    import oracle as O
+
+    x = O.rng(seed, 0).integers(-127, 128, COLS, dtype=np.int8)
+    w = O.rng(seed, 1).integers(0, 256, (ROWS, COLS // 2), dtype=np.uint8)
+    s16 = O.rng(seed, 2).uniform(1e-3, 1e-2, (ROWS, COLS // GROUP)).astype(np.float16)
+    return x, w, s16
+
+
+def cpu_reference_runner():
+    """(run_one_gemv, kind, threads): the reference C on row slices across threads."""
+    import oracle as O
+
+    x, w, s16 = make_host_inputs()
+    s32 = s16.astype(np.float32)
+    y = np.zeros(ROWS, np.float32)
+    if O.ref_available("generic"):
+        impl, kind = O.RefLib("generic"), "reference"
+        fn = impl.lib.ks_matvec_w4a8
+        call = lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
+                                s32.ctypes.data + r0 * s32.strides[0], s32.shape[1], y.ctypes.data + 4 * r0,
+                                n, COLS, GROUP, SX, 0, 0, None, 0)
+    else:
+        impl, kind = O.Oracle(), "port"
+        fn = impl.lib.kso_matvec_w4a8
+        call = lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
+                                s32.ctypes.data + r0 * s32.strides[0], s32.shape[1], y.ctypes.data + 4 * r0,
+                                n, COLS, GROUP, SX, 0, 0)
+    T = host_threads()
+    bounds = [(ROWS * i // T, ROWS * (i + 1) // T) for i in range(T)]
+    bounds = [(a, b - a) for a, b in bounds if b > a]
+    pool = cf.ThreadPoolExecutor(max_workers=len(bounds))
+
+    def one():
+        rcs = list(pool.map(lambda ab: call(*ab), bounds))
+        assert all(rc == 0 for rc in rcs), rcs
+
+    return one, kind, len(bounds), pool
+
+
+def time_cpu_reference(n_gemvs: int, warmup: int = 1):
+    one, kind, threads, pool = cpu_reference_runner()
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(n_gemvs):
+        one()
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    return dt, kind, threads
+
+
+def run_reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    one, kind, threads, pool = cpu_reference_runner()
+    for _ in range(args.warmup):
+        one()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    pool.shutdown()
+    total = sum(times)
+    value = gemv_bytes() * args.steps / total / 1e12
+    sample = (f"1 GEMV {ROWS}x{COLS} G{GROUP} per step (f32 scales widened from the f16 set), rows split over "
+              f"{threads} threads, reference ks_matvec_w4a8 ({'oracle/_ref generic -O3' if kind == 'reference' else 'oracle port'})")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a8-f32acc",
+        "data": "synthetic (seeded)", "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(world):
+    return {
+        "workload": f"w4a8_gemv rows={ROWS} cols={COLS} group={GROUP} f16 scales; {MATS} resident matrices per step",
+        "rows_per_gpu": ROWS, "cols": COLS, "group": GROUP, "scale_dtype": "f16", "gemvs_per_step": MATS,
+        "global_rows": ROWS * world, "parallelism": "row-shard + NCCL all-gather" if world > 1 else "single GPU",
+        "l2": f"inputs {MATS * gemv_bytes() / 1e9:.2f} GB per GPU > 126 MB L2; no flush",
+        "bytes_per_gemv": gemv_bytes(),
+    }
+
+
+# ------------------------------------------------------------ clocks (NVML) --
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Polls SM clock and clock-event reasons of this rank's GPU via NVML."""
+
+    def __init__(self, torch_device):
+        self.samples = []
+        self.ok = False
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(torch_device).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.ok = True
+        except Exception as e:  # pragma: no cover - NVML missing
+            self.err = repr(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                sm = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = int(self._reasons(self.h))
+                self.samples.append((sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": getattr(self, "max_mhz", None), "reasons": [],
+                    "samples": 0, "note": getattr(self, "err", "no samples")}
+        mhz = [s for s, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = [name for bit, name in REASON_BITS.items() if bits & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "NVML (same counters as nvidia-smi)"}
+
+
+# ---------------------------------------------------------------- B200 arm --
+def run_b200_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import kernelsmith_b200 as K
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    L = K.lib()
+
+    # ---- resident inputs: 64 shards of [ROWS, COLS] (this rank's rows) ----
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 7919 * rank)
+    W = torch.randint(0, 256, (MATS, ROWS, COLS // 2), dtype=torch.uint8, device=dev, generator=gen)
+    S = (torch.rand((MATS, ROWS, COLS // GROUP), device=dev, generator=gen) * 9e-3 + 1e-3).to(torch.float16)
+    X = torch.randint(-127, 128, (MATS, COLS), dtype=torch.int8, device=dev, generator=gen)
+    Yfull = torch.zeros((CHUNKS, world, MATS // CHUNKS, ROWS), dtype=torch.float32, device=dev)
+    Yloc = torch.zeros((CHUNKS, MATS // CHUNKS, ROWS), dtype=torch.float32, device=dev)
+    status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
+    assert L.ks_b200_w4a8_kernel_path(X.data_ptr(), W.data_ptr(), COLS // 2, S.data_ptr(), K.SCALE_F16,
+                                      COLS // GROUP, ROWS, COLS, GROUP) == 1
+
+    main = torch.cuda.Stream(device=dev)
+    comm = torch.cuda.Stream(device=dev)
+    per_chunk = MATS // CHUNKS
+
+    def gemv_chunk(c):
+        for j in range(per_chunk):
+            m = c * per_chunk + j
+            K.matvec_w4a8_async(X[m], W[m], COLS // 2, S[m], COLS // GROUP, Yloc[c, j], ROWS, COLS, GROUP, SX,
+                                scale_type=K.SCALE_F16, status=status, stream=main)
+
+    # one CUDA graph per chunk of 16 GEMVs (launch-bound inner loop)
+    graphs = []
+    with torch.cuda.stream(main):
+        for c in range(CHUNKS):
+            gemv_chunk(c)  # warm-up / attribute setup outside capture
+    main.synchronize()
+    for c in range(CHUNKS):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=main):
+            gemv_chunk(c)
+        graphs.append(g)
+
+    def step():
+        for c in range(CHUNKS):
+            graphs[c].replay()
+            if world > 1:
+                ev = torch.cuda.Event()
+                ev.record(main)
+                comm.wait_event(ev)
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(Yfull[c], Yloc[c])
+        if world > 1:
+            main.wait_stream(comm)
+
+    with torch.cuda.stream(main):
+        for _ in range(max(3, args.warmup)):
+            step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks, torch.cuda.stream(main):
+        start.record(main)
+        for _ in range(args.steps):
+            step()
+        end.record(main)
+        end.synchronize()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    st = status.cpu().tolist()
+    assert st == [0, 0], f"device status {st}"
+
+    total_bytes = gemv_bytes() * MATS * args.steps * world
+    value = total_bytes / (ms * 1e-3) / 1e12
+    per_launch_s = ms * 1e-3 / (MATS * args.steps)
+    peak, peak_kind = measured_hbm_peak()
+    achieved = gemv_bytes() / per_launch_s / 1e9
+
+    # ---- e2e: public synchronous C ABI with pinned host buffers ----------
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(1, min(args.steps, 5))
+    e2e = run_e2e(L, K, torch, dist, dev, world, rank, e2e_steps)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n = MATS
+        dt, kind, threads = time_cpu_reference(n)
+        cpu = {"value": gemv_bytes() * n / dt / 1e12, "unit": "TB/s", "cores": threads, "kind": kind,
+               "sample": f"{n} GEMVs {ROWS}x{COLS} G{GROUP} (one step), f32 scales, rows split over {threads} "
+                         f"threads, {dt:.2f} s wall"}
+
+    for g in graphs:
+        del g
+    graphs.clear()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "w4a8-i32acc-f32out",
+            "data": "synthetic (seeded uniform int4 / int8, f16 scales U[1e-3,1e-2])",
+            "config": workload_config(world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "kernel": "gemv_stream_kernel<W4A8Op<__half,4>>",
+                         "bytes_per_launch": gemv_bytes(), "launch_us": per_launch_s * 1e6},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": MATS * args.steps * world,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(L, K, torch, dist, dev, world, rank, steps):
+    """Host buffers through ks_b200_matvec_w4a8_f16: H2D + kernel + D2H per GEMV."""
+    nbuf = 4
+    x, w, s16 = make_host_inputs(SEED + rank)
+    hw = [torch.from_numpy(w).pin_memory() for _ in range(nbuf)]
+    hs = [torch.from_numpy(s16.view(np.uint16)).pin_memory() for _ in range(nbuf)]
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.zeros((MATS, ROWS), dtype=torch.float32).pin_memory()
+    gathered = torch.zeros((world, ROWS), dtype=torch.float32, device=dev) if world > 1 else None
+
+    def one_step():
+        for m in range(MATS):
+            rc = L.ks_b200_matvec_w4a8_f16(hx.data_ptr(), hw[m % nbuf].data_ptr(), COLS // 2,
+                                           hs[m % nbuf].data_ptr(), COLS // GROUP, hy[m].data_ptr(), ROWS, COLS,
+                                           GROUP, SX, 0, 0)
+            K.check(rc)
+        if world > 1:  # the step's output slices, exchanged (device round trip)
+            dist.all_gather_into_tensor(gathered, hy[MATS - 1].to(dev, non_blocking=False))
+            torch.cuda.synchronize()
+
+    one_step()  # warm-up (staging buffers)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_step()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([dt], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    h2d = MATS * (w.nbytes + s16.nbytes + x.nbytes)
+    d2h = MATS * ROWS * 4
+    return {"value": gemv_bytes() * MATS * steps * world / dt / 1e12, "unit": "TB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "api": "ks_b200_matvec_w4a8_f16 (synchronous C ABI), pinned host buffers"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_b200_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,134 @@
+/*
+ * ks_b200.h -- B200 extensions to the libkernelsmith quantized C API.
+ *
+ * The reference library (pkp124/ulir-kernels) has no counterpart for any
+ * declaration in this file; each one composes reference semantics that the
+ * comment names.  The reference entry points themselves are declared,
+ * unchanged, in kernelsmith/ks_quantized.h and kernelsmith/ks_common.h, which
+ * this header includes.
+ *
+ * Two calling conventions:
+ *   synchronous  (no suffix)   same as ks_quantized.h: device, managed or
+ *                              host pointers; returns when the output is
+ *                              written; bad scales reported as
+ *                              KS_ERR_INVALID_ARG.
+ *   asynchronous (_async)      device (or managed) pointers only; the kernel
+ *                              is queued on `stream` (a cudaStream_t, NULL for
+ *                              the legacy default stream) and the call
+ *                              returns at once.  Host-side argument checks
+ *                              still return KS_ERR_INVALID_ARG.  Device-side
+ *                              findings are written to `status` (device-
+ *                              accessible memory holding
+ *                              KS_B200_STATUS_WORDS uint32 words, cleared by
+ *                              the caller; NULL to skip): word 0 becomes 1 if a
+ *                              weight scale is <= 0, inf or nan, word 1 if a
+ *                              device-side wait hit its one-second limit.
+ *                              Nothing is allocated; the calls can be captured
+ *                              in a CUDA graph.
+ */
+
+#ifndef KS_B200_H
+#define KS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "kernelsmith/ks_common.h"
+#include "kernelsmith/ks_quantized.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A CUDA error or a device-side timeout.  ks_b200_last_error() says which. */
+#define KS_ERR_DEVICE (-4)
+
+/* Scale element types for the *_async W4A8 entry points. */
+#define KS_B200_SCALE_F32 0
+#define KS_B200_SCALE_F16 1
+
+#define KS_B200_STATUS_WORDS 2
+#define KS_B200_STATUS_BAD_SCALE 0
+#define KS_B200_STATUS_TIMEOUT 1
+
+/* "major.minor.patch+sm_100a" of this build. */
+const char *ks_b200_version(void);
+
+/* Message of the last failing call made by this thread ("" if none). */
+const char *ks_b200_last_error(void);
+
+/* Number of CUDA devices visible to the process (0 without a GPU). */
+int ks_b200_device_count(void);
+
+/*
+ * ks_matvec_w4a8 with IEEE binary16 group scales (the raw 16-bit patterns).
+ * Each half widens exactly to f32, then the contract of ks_matvec_w4a8
+ * applies unchanged, validation included.  Halves the scale traffic of the
+ * f32 form.  Composes reference ks_quantized.c:94-159 with an exact
+ * f16 -> f32 conversion.
+ */
+int ks_b200_matvec_w4a8_f16(const int8_t *input, const uint8_t *packed_weights,
+                            size_t packed_stride_bytes,
+                            const uint16_t *weight_scales_f16,
+                            size_t scale_stride, float *output, size_t rows,
+                            size_t cols, size_t group_size, float input_scale,
+                            int32_t input_zero_point,
+                            int32_t weight_zero_point);
+
+/*
+ * INT8 GEMV with a per-output-channel dequant epilogue:
+ *   output[r] = (f32(acc[r]) * weight_scales[r]) * input_scale
+ * where acc[r] is exactly ks_matvec_i8's int32 result; each product is one
+ * IEEE round-to-nearest multiply in the order written (no fused multiply-add),
+ * so results are bit-exact against the same expression on the CPU.
+ * Argument checks are ks_matvec_i8's plus weight_scales != NULL.
+ */
+int ks_b200_matvec_i8_dequant(const int8_t *input, const int8_t *weights,
+                              size_t weight_stride, const float *weight_scales,
+                              float input_scale, float *output, size_t rows,
+                              size_t cols, int32_t input_zero_point,
+                              int32_t weight_zero_point);
+
+/* Asynchronous forms (device pointers, caller's stream, no allocation). */
+int ks_b200_matvec_w4a8_async(const int8_t *input,
+                              const uint8_t *packed_weights,
+                              size_t packed_stride_bytes,
+                              const void *weight_scales, int scale_type,
+                              size_t scale_stride, float *output, size_t rows,
+                              size_t cols, size_t group_size,
+                              float input_scale, int32_t input_zero_point,
+                              int32_t weight_zero_point, uint32_t *status,
+                              void *stream);
+
+int ks_b200_matvec_i8_async(const int8_t *input, const int8_t *weights,
+                            size_t weight_stride, int32_t *output, size_t rows,
+                            size_t cols, int32_t input_zero_point,
+                            int32_t weight_zero_point, void *stream);
+
+int ks_b200_matvec_i8_dequant_async(const int8_t *input, const int8_t *weights,
+                                    size_t weight_stride,
+                                    const float *weight_scales,
+                                    float input_scale, float *output,
+                                    size_t rows, size_t cols,
+                                    int32_t input_zero_point,
+                                    int32_t weight_zero_point, void *stream);
+
+/*
+ * Which kernel family a W4A8 / INT8 call with these arguments runs on the
+ * current device: 1 = TMA-staged streaming kernel, 0 = generic per-element
+ * kernel (any stride, alignment, odd cols, any group size), negative = the
+ * arguments would be rejected.  For tests and benchmarks.
+ */
+int ks_b200_w4a8_kernel_path(const void *input, const void *packed_weights,
+                             size_t packed_stride_bytes,
+                             const void *weight_scales, int scale_type,
+                             size_t scale_stride, size_t rows, size_t cols,
+                             size_t group_size);
+int ks_b200_i8_kernel_path(const void *input, const void *weights,
+                           size_t weight_stride, size_t rows, size_t cols);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KS_B200_H */

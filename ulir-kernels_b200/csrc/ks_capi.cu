@@ -1,0 +1,528 @@
+// ks_capi.cu -- the libkernelsmith C ABI on B200.
+//
+// Exports every function of kernelsmith/ks_quantized.h and
+// kernelsmith/ks_common.h with the reference signatures, plus the extensions
+// of ks_b200.h.  Host-side argument checks run first, in the order of the
+// reference C (lib/kernelsmith/ks_quantized.c), so an invalid call returns
+// the same code without touching the GPU.  Scale validity is checked by the
+// kernels while they read the scales and reported through a status word.
+//
+// There is no CPU fallback: if no CUDA device can run the kernels, compute
+// calls return KS_ERR_DEVICE.
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "ks_b200.h"
+#include "ks_internal.h"
+#include "b200_sm100a.h"
+
+namespace ksb {
+namespace {
+
+constexpr int kMaxDevices = 64;
+enum Slot { kSlotX = 0, kSlotW, kSlotS, kSlotY, kSlots };
+
+struct ThreadState {
+  uint32_t *status = nullptr;  // mapped, portable pinned host memory
+  struct Buf {
+    void *p = nullptr;
+    size_t n = 0;
+  } bufs[kMaxDevices][kSlots];
+  std::string err;
+  ~ThreadState() {
+    for (int d = 0; d < kMaxDevices; ++d)
+      for (int s = 0; s < kSlots; ++s)
+        if (bufs[d][s].p) {
+          cudaSetDevice(d);
+          cudaFree(bufs[d][s].p);
+        }
+    if (status) cudaFreeHost(status);
+  }
+};
+
+ThreadState &tls() {
+  thread_local ThreadState ts;
+  return ts;
+}
+
+int fail(int code, const std::string &msg) {
+  tls().err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+  cudaGetLastError();
+  return fail(KS_ERR_DEVICE, m);
+}
+
+bool i8_zp_ok(int32_t z) { return z >= -128 && z <= 127; }
+bool i4_zp_ok(int32_t z) { return z >= -8 && z <= 7; }
+bool pos_finite(float v) { return v > 0.0f && std::isfinite(v); }
+
+size_t packed_row_bytes(size_t cols) { return cols / 2 + (cols & 1); }
+size_t scale_groups(size_t cols, size_t g) { return g == 0 ? 0 : cols / g + (cols % g != 0); }
+
+// Where a caller's buffer lives.
+struct Where {
+  bool device = false;
+  int dev = -1;
+};
+
+Where classify(const void *p) {
+  Where w;
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return w;
+  }
+  if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+    w.device = true;
+    w.dev = at.device;
+  }
+  return w;
+}
+
+// A synchronous call's buffers, resolved to device addresses.
+class SyncCall {
+ public:
+  // Pick the device from the device-resident buffers (all must agree) or the
+  // thread's current device, and make it current.
+  int begin(const void *const *ptrs, int n) {
+    int devcount = 0;
+    cudaError_t e = cudaGetDeviceCount(&devcount);
+    if (e != cudaSuccess || devcount == 0) {
+      cudaGetLastError();
+      return fail(KS_ERR_DEVICE, "no CUDA device available for the B200 kernels");
+    }
+    dev_ = -1;
+    for (int i = 0; i < n; ++i) {
+      where_[i] = classify(ptrs[i]);
+      if (where_[i].device) {
+        if (dev_ >= 0 && where_[i].dev != dev_)
+          return fail(KS_ERR_INVALID_ARG, "buffers live on different devices");
+        dev_ = where_[i].dev;
+      }
+    }
+    if (dev_ < 0 && (e = cudaGetDevice(&dev_)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev_ >= kMaxDevices) return fail(KS_ERR_DEVICE, "device index out of range");
+    if ((e = cudaSetDevice(dev_)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    const DeviceProps &dp = device_props(dev_);
+    if (dp.cc_major != 10) return fail(KS_ERR_DEVICE, "libkernelsmith (B200) needs an sm_100 device");
+    ThreadState &ts = tls();
+    if (!ts.status) {
+      void *p = nullptr;
+      e = cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(status)");
+      ts.status = static_cast<uint32_t *>(p);
+    }
+    ts.status[kStatusBadScale] = 0;
+    ts.status[kStatusTimeout] = 0;
+    e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&status_dev_), ts.status, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer(status)");
+    return KS_OK;
+  }
+
+  // Device address for buffer i of `bytes` bytes; host buffers are staged
+  // (inputs copied in now, outputs copied back by finish()).
+  int map(int i, int slot, const void *host, size_t bytes, bool input, void **out) {
+    if (where_[i].device || bytes == 0) {
+      *out = const_cast<void *>(host);
+      return KS_OK;
+    }
+    ThreadState::Buf &b = tls().bufs[dev_][slot];
+    if (b.n < bytes) {
+      if (b.p) cudaFree(b.p);
+      b.p = nullptr;
+      b.n = 0;
+      cudaError_t e = cudaMalloc(&b.p, bytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
+      b.n = bytes;
+    }
+    if (input) {
+      cudaError_t e = cudaMemcpyAsync(b.p, host, bytes, cudaMemcpyHostToDevice, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(H2D)");
+    } else {
+      copy_back_host_ = const_cast<void *>(host);
+      copy_back_dev_ = b.p;
+      copy_back_bytes_ = bytes;
+    }
+    *out = b.p;
+    return KS_OK;
+  }
+
+  int device() const { return dev_; }
+  uint32_t *status_dev() const { return status_dev_; }
+
+  // Copy staged outputs back, wait, and turn device status into a code.
+  int finish(cudaError_t launch_err) {
+    if (launch_err != cudaSuccess) return cuda_fail(launch_err, "kernel launch");
+    cudaError_t e;
+    if (copy_back_host_) {
+      e = cudaMemcpyAsync(copy_back_host_, copy_back_dev_, copy_back_bytes_, cudaMemcpyDeviceToHost, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(D2H)");
+    }
+    e = cudaStreamSynchronize(0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    const volatile uint32_t *st = tls().status;
+    if (st[kStatusTimeout]) return fail(KS_ERR_DEVICE, "a device-side wait timed out");
+    if (st[kStatusBadScale]) return fail(KS_ERR_INVALID_ARG, "a weight scale is <= 0, inf or nan");
+    return KS_OK;
+  }
+
+ private:
+  Where where_[8];
+  int dev_ = -1;
+  uint32_t *status_dev_ = nullptr;
+  void *copy_back_host_ = nullptr;
+  void *copy_back_dev_ = nullptr;
+  size_t copy_back_bytes_ = 0;
+};
+
+// Write a scalar result of a zero-length dot to a device or host pointer.
+int write_scalar(void *out, const void *value, size_t bytes) {
+  int devcount = 0;
+  if (cudaGetDeviceCount(&devcount) != cudaSuccess) cudaGetLastError();
+  if (devcount > 0 && classify(out).device) {
+    cudaError_t e = cudaMemcpy(out, value, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(scalar)");
+  } else {
+    std::memcpy(out, value, bytes);
+  }
+  return KS_OK;
+}
+
+// ------------------------------------------------------------- W4A8 core --
+int w4a8_sync(const int8_t *x, const uint8_t *w, size_t wstride, const void *s, int stype,
+              size_t sstride, float *y, size_t rows, size_t cols, size_t group, float sx,
+              int32_t zx, int32_t zw) {
+  const size_t ssize = stype == kScaleF16 ? 2 : 4;
+  const size_t groups = scale_groups(cols, group);
+  SyncCall call;
+  const void *ptrs[4] = {x, w, s, y};
+  int rc = call.begin(ptrs, 4);
+  if (rc != KS_OK) return rc;
+  void *dx = nullptr, *dw = nullptr, *ds = nullptr, *dy = nullptr;
+  const size_t wbytes = (rows - 1) * wstride + packed_row_bytes(cols);
+  const size_t sbytes = ((rows - 1) * sstride + groups) * ssize;
+  if ((rc = call.map(0, kSlotX, x, cols, true, &dx)) != KS_OK) return rc;
+  if ((rc = call.map(1, kSlotW, w, wbytes, true, &dw)) != KS_OK) return rc;
+  if ((rc = call.map(2, kSlotS, s, sbytes, true, &ds)) != KS_OK) return rc;
+  if ((rc = call.map(3, kSlotY, y, rows * sizeof(float), false, &dy)) != KS_OK) return rc;
+  W4A8Launch a{};
+  a.x = static_cast<const int8_t *>(dx);
+  a.w = static_cast<const uint8_t *>(dw);
+  a.wstride = (int64_t)wstride;
+  a.s = ds;
+  a.sstride = (int64_t)sstride;
+  a.stype = stype;
+  a.y = static_cast<float *>(dy);
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group;
+  a.sx = sx;
+  a.zx = zx;
+  a.zw = zw;
+  a.status = call.status_dev();
+  return call.finish(launch_w4a8(a, 0, call.device()));
+}
+
+// Checks of ks_matvec_w4a8 (ks_quantized.c:138-146) followed by the per-row
+// checks of ks_dot_w4a8 that do not depend on the row (:100-110).
+int w4a8_matvec_checks(const int8_t *x, const uint8_t *w, size_t wstride, const void *s,
+                       size_t sstride, const float *y, size_t rows, size_t cols, size_t group,
+                       float sx, int32_t zx, int32_t zw) {
+  if (!x || !w || !s || !y) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (rows == 0 || cols == 0 || group == 0) return fail(KS_ERR_INVALID_ARG, "rows, cols and group_size must be > 0");
+  if (wstride < packed_row_bytes(cols) || sstride < scale_groups(cols, group))
+    return fail(KS_ERR_INVALID_ARG, "stride smaller than one row");
+  if (!pos_finite(sx)) return fail(KS_ERR_INVALID_ARG, "input_scale must be > 0 and finite");
+  if (!i8_zp_ok(zx) || !i4_zp_ok(zw)) return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  return KS_OK;
+}
+
+int i8_sync(const int8_t *x, const int8_t *w, size_t wstride, void *y, size_t rows, size_t cols,
+            int32_t zx, int32_t zw, const float *ws, float sa, bool out_f32) {
+  SyncCall call;
+  const void *ptrs[4] = {x, w, y, ws ? static_cast<const void *>(ws) : static_cast<const void *>(x)};
+  int rc = call.begin(ptrs, 4);
+  if (rc != KS_OK) return rc;
+  void *dx = nullptr, *dw = nullptr, *dy = nullptr, *dws = nullptr;
+  const size_t wbytes = (rows - 1) * wstride + cols;
+  if ((rc = call.map(0, kSlotX, x, cols, true, &dx)) != KS_OK) return rc;
+  if ((rc = call.map(1, kSlotW, w, wbytes, true, &dw)) != KS_OK) return rc;
+  if (out_f32 && (rc = call.map(3, kSlotS, ws, rows * sizeof(float), true, &dws)) != KS_OK) return rc;
+  if ((rc = call.map(2, kSlotY, y, rows * 4, false, &dy)) != KS_OK) return rc;
+  I8Launch a{};
+  a.x = static_cast<const int8_t *>(dx);
+  a.w = static_cast<const int8_t *>(dw);
+  a.wstride = (int64_t)wstride;
+  a.y = dy;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.zx = zx;
+  a.zw = zw;
+  a.ws = static_cast<const float *>(dws);
+  a.sa = sa;
+  a.out_f32 = out_f32 ? 1 : 0;
+  a.status = call.status_dev();
+  return call.finish(launch_i8(a, 0, call.device()));
+}
+
+int current_device(int *dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(KS_ERR_DEVICE, "device index out of range");
+  return KS_OK;
+}
+
+}  // namespace
+
+void set_last_error(const std::string &msg) { tls().err = msg; }
+
+}  // namespace ksb
+
+using namespace ksb;
+
+// ================================================================ ks_common
+extern "C" const char *ks_target_name(void) { return KS_TARGET_NAME; }
+extern "C" size_t ks_simd_width_f32(void) { return KS_SIMD_WIDTH_F32; }
+
+// ============================================================= ks_quantized
+extern "C" int ks_dot_i8(const int8_t *input, const int8_t *weight, size_t k,
+                         int32_t input_zero_point, int32_t weight_zero_point, int32_t *output,
+                         void *workspace, size_t ws_size) {
+  (void)workspace;
+  (void)ws_size;
+  if (!input || !weight || !output) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (!i8_zp_ok(input_zero_point) || !i8_zp_ok(weight_zero_point))
+    return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  if (k == 0) {
+    const int32_t zero = 0;
+    return write_scalar(output, &zero, sizeof zero);
+  }
+  return i8_sync(input, weight, k, output, 1, k, input_zero_point, weight_zero_point, nullptr,
+                 0.0f, false);
+}
+
+extern "C" int ks_matvec_i8(const int8_t *input, const int8_t *weights, size_t weight_stride,
+                            int32_t *output, size_t rows, size_t cols, int32_t input_zero_point,
+                            int32_t weight_zero_point, void *workspace, size_t ws_size) {
+  (void)workspace;
+  (void)ws_size;
+  if (!input || !weights || !output) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (rows == 0 || cols == 0 || weight_stride < cols)
+    return fail(KS_ERR_INVALID_ARG, "rows/cols must be > 0 and weight_stride >= cols");
+  if (!i8_zp_ok(input_zero_point) || !i8_zp_ok(weight_zero_point))
+    return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  return i8_sync(input, weights, weight_stride, output, rows, cols, input_zero_point,
+                 weight_zero_point, nullptr, 0.0f, false);
+}
+
+extern "C" int ks_dot_w4a8(const int8_t *input, const uint8_t *packed_weight,
+                           const float *weight_scales, size_t k, size_t group_size,
+                           float input_scale, int32_t input_zero_point, int32_t weight_zero_point,
+                           float *output, void *workspace, size_t ws_size) {
+  (void)workspace;
+  (void)ws_size;
+  if (!input || !packed_weight || !weight_scales || !output) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (group_size == 0) return fail(KS_ERR_INVALID_ARG, "group_size must be > 0");
+  if (!pos_finite(input_scale)) return fail(KS_ERR_INVALID_ARG, "input_scale must be > 0 and finite");
+  if (!i8_zp_ok(input_zero_point) || !i4_zp_ok(weight_zero_point))
+    return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  if (k == 0) {
+    const float zero = 0.0f;
+    return write_scalar(output, &zero, sizeof zero);
+  }
+  return w4a8_sync(input, packed_weight, packed_row_bytes(k), weight_scales, kScaleF32,
+                   scale_groups(k, group_size), output, 1, k, group_size, input_scale,
+                   input_zero_point, weight_zero_point);
+}
+
+extern "C" int ks_matvec_w4a8(const int8_t *input, const uint8_t *packed_weights,
+                              size_t packed_stride_bytes, const float *weight_scales,
+                              size_t scale_stride, float *output, size_t rows, size_t cols,
+                              size_t group_size, float input_scale, int32_t input_zero_point,
+                              int32_t weight_zero_point, void *workspace, size_t ws_size) {
+  (void)workspace;
+  (void)ws_size;
+  int rc = w4a8_matvec_checks(input, packed_weights, packed_stride_bytes, weight_scales,
+                              scale_stride, output, rows, cols, group_size, input_scale,
+                              input_zero_point, weight_zero_point);
+  if (rc != KS_OK) return rc;
+  return w4a8_sync(input, packed_weights, packed_stride_bytes, weight_scales, kScaleF32,
+                   scale_stride, output, rows, cols, group_size, input_scale, input_zero_point,
+                   weight_zero_point);
+}
+
+extern "C" size_t ks_dot_i8_workspace(size_t k) { return KS_QUANT_DOT_I8_WORKSPACE_BYTES(k); }
+extern "C" size_t ks_matvec_i8_workspace(size_t rows, size_t cols) {
+  return KS_QUANT_MATVEC_I8_WORKSPACE_BYTES(rows, cols);
+}
+extern "C" size_t ks_dot_w4a8_workspace(size_t k, size_t group_size) {
+  return KS_QUANT_DOT_W4A8_WORKSPACE_BYTES(k, group_size);
+}
+extern "C" size_t ks_matvec_w4a8_workspace(size_t rows, size_t cols, size_t group_size) {
+  return KS_QUANT_MATVEC_W4A8_WORKSPACE_BYTES(rows, cols, group_size);
+}
+extern "C" size_t ks_quantized_alignment(void) { return KS_PREFERRED_ALIGN; }
+extern "C" size_t ks_w4a8_packed_row_bytes(size_t cols) { return packed_row_bytes(cols); }
+extern "C" size_t ks_w4a8_scale_groups(size_t cols, size_t group_size) {
+  return scale_groups(cols, group_size);
+}
+
+// ================================================================ ks_b200.h
+extern "C" const char *ks_b200_version(void) { return KS_B200_VERSION_STRING; }
+extern "C" const char *ks_b200_last_error(void) { return tls().err.c_str(); }
+
+extern "C" int ks_b200_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+extern "C" int ks_b200_matvec_w4a8_f16(const int8_t *input, const uint8_t *packed_weights,
+                                       size_t packed_stride_bytes, const uint16_t *weight_scales_f16,
+                                       size_t scale_stride, float *output, size_t rows, size_t cols,
+                                       size_t group_size, float input_scale,
+                                       int32_t input_zero_point, int32_t weight_zero_point) {
+  int rc = w4a8_matvec_checks(input, packed_weights, packed_stride_bytes, weight_scales_f16,
+                              scale_stride, output, rows, cols, group_size, input_scale,
+                              input_zero_point, weight_zero_point);
+  if (rc != KS_OK) return rc;
+  return w4a8_sync(input, packed_weights, packed_stride_bytes, weight_scales_f16, kScaleF16,
+                   scale_stride, output, rows, cols, group_size, input_scale, input_zero_point,
+                   weight_zero_point);
+}
+
+extern "C" int ks_b200_matvec_i8_dequant(const int8_t *input, const int8_t *weights,
+                                         size_t weight_stride, const float *weight_scales,
+                                         float input_scale, float *output, size_t rows, size_t cols,
+                                         int32_t input_zero_point, int32_t weight_zero_point) {
+  if (!input || !weights || !output || !weight_scales) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (rows == 0 || cols == 0 || weight_stride < cols)
+    return fail(KS_ERR_INVALID_ARG, "rows/cols must be > 0 and weight_stride >= cols");
+  if (!i8_zp_ok(input_zero_point) || !i8_zp_ok(weight_zero_point))
+    return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  return i8_sync(input, weights, weight_stride, output, rows, cols, input_zero_point,
+                 weight_zero_point, weight_scales, input_scale, true);
+}
+
+extern "C" int ks_b200_matvec_w4a8_async(const int8_t *input, const uint8_t *packed_weights,
+                                         size_t packed_stride_bytes, const void *weight_scales,
+                                         int scale_type, size_t scale_stride, float *output,
+                                         size_t rows, size_t cols, size_t group_size,
+                                         float input_scale, int32_t input_zero_point,
+                                         int32_t weight_zero_point, uint32_t *status, void *stream) {
+  if (scale_type != kScaleF32 && scale_type != kScaleF16)
+    return fail(KS_ERR_INVALID_ARG, "unknown scale_type");
+  int rc = w4a8_matvec_checks(input, packed_weights, packed_stride_bytes, weight_scales,
+                              scale_stride, output, rows, cols, group_size, input_scale,
+                              input_zero_point, weight_zero_point);
+  if (rc != KS_OK) return rc;
+  int dev;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  W4A8Launch a{};
+  a.x = input;
+  a.w = packed_weights;
+  a.wstride = (int64_t)packed_stride_bytes;
+  a.s = weight_scales;
+  a.sstride = (int64_t)scale_stride;
+  a.stype = scale_type;
+  a.y = output;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group_size;
+  a.sx = input_scale;
+  a.zx = input_zero_point;
+  a.zw = weight_zero_point;
+  a.status = status;
+  cudaError_t e = launch_w4a8(a, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+static int i8_async(const int8_t *input, const int8_t *weights, size_t weight_stride, void *output,
+                    size_t rows, size_t cols, int32_t zx, int32_t zw, const float *ws, float sa,
+                    bool out_f32, void *stream) {
+  if (!input || !weights || !output || (out_f32 && !ws)) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (rows == 0 || cols == 0 || weight_stride < cols)
+    return fail(KS_ERR_INVALID_ARG, "rows/cols must be > 0 and weight_stride >= cols");
+  if (!i8_zp_ok(zx) || !i8_zp_ok(zw)) return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  I8Launch a{};
+  a.x = input;
+  a.w = weights;
+  a.wstride = (int64_t)weight_stride;
+  a.y = output;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.zx = zx;
+  a.zw = zw;
+  a.ws = ws;
+  a.sa = sa;
+  a.out_f32 = out_f32 ? 1 : 0;
+  a.status = nullptr;
+  cudaError_t e = launch_i8(a, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_matvec_i8_async(const int8_t *input, const int8_t *weights,
+                                       size_t weight_stride, int32_t *output, size_t rows,
+                                       size_t cols, int32_t input_zero_point,
+                                       int32_t weight_zero_point, void *stream) {
+  return i8_async(input, weights, weight_stride, output, rows, cols, input_zero_point,
+                  weight_zero_point, nullptr, 0.0f, false, stream);
+}
+
+extern "C" int ks_b200_matvec_i8_dequant_async(const int8_t *input, const int8_t *weights,
+                                               size_t weight_stride, const float *weight_scales,
+                                               float input_scale, float *output, size_t rows,
+                                               size_t cols, int32_t input_zero_point,
+                                               int32_t weight_zero_point, void *stream) {
+  return i8_async(input, weights, weight_stride, output, rows, cols, input_zero_point,
+                  weight_zero_point, weight_scales, input_scale, true, stream);
+}
+
+extern "C" int ks_b200_w4a8_kernel_path(const void *input, const void *packed_weights,
+                                        size_t packed_stride_bytes, const void *weight_scales,
+                                        int scale_type, size_t scale_stride, size_t rows,
+                                        size_t cols, size_t group_size) {
+  if (rows == 0 || cols == 0 || group_size == 0) return -1;
+  if (packed_stride_bytes < packed_row_bytes(cols) || scale_stride < scale_groups(cols, group_size))
+    return -1;
+  if (ks_b200_device_count() == 0) return -1;
+  W4A8Launch a{};
+  a.x = static_cast<const int8_t *>(input);
+  a.w = static_cast<const uint8_t *>(packed_weights);
+  a.wstride = (int64_t)packed_stride_bytes;
+  a.s = weight_scales;
+  a.sstride = (int64_t)scale_stride;
+  a.stype = scale_type;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group_size;
+  return w4a8_path(a);
+}
+
+extern "C" int ks_b200_i8_kernel_path(const void *input, const void *weights, size_t weight_stride,
+                                      size_t rows, size_t cols) {
+  if (rows == 0 || cols == 0 || weight_stride < cols) return -1;
+  if (ks_b200_device_count() == 0) return -1;
+  I8Launch a{};
+  a.x = static_cast<const int8_t *>(input);
+  a.w = static_cast<const int8_t *>(weights);
+  a.wstride = (int64_t)weight_stride;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  return i8_path(a);
+}

@@ -1,0 +1,82 @@
+// ks_internal.h -- host-side declarations shared by the libkernelsmith (B200)
+// translation units: kernel launchers, device properties, error text.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+namespace ksb {
+
+enum ScaleType : int { kScaleF32 = 0, kScaleF16 = 1 };
+
+// Status words written by kernels (plain stores of 1, never atomics, so the
+// words may live in mapped host memory).  status[0]: a weight scale was <= 0,
+// inf or nan.  status[1]: a device-side wait hit its time limit.
+constexpr int kStatusBadScale = 0;
+constexpr int kStatusTimeout = 1;
+constexpr int kStatusWords = 2;
+
+struct W4A8Launch {
+  const int8_t *x;
+  const uint8_t *w;
+  int64_t wstride;  // bytes between packed rows
+  const void *s;    // f32 or f16 group scales
+  int64_t sstride;  // scale elements between rows
+  int stype;        // ScaleType
+  float *y;
+  int64_t rows, cols, group;
+  float sx;
+  int32_t zx, zw;
+  uint32_t *status;  // kStatusWords words, may be null
+};
+
+struct I8Launch {
+  const int8_t *x;
+  const int8_t *w;
+  int64_t wstride;  // bytes between rows
+  void *y;          // int32_t[rows] or float[rows]
+  int64_t rows, cols;
+  int32_t zx, zw;
+  const float *ws;  // per-row dequant scale (f32 output only)
+  float sa;         // activation scale (f32 output only)
+  int out_f32;
+  uint32_t *status;
+};
+
+struct GemmI8Launch {
+  const int8_t *a;   // [m, k], row stride lda
+  int64_t lda;
+  const float *sa;   // [m]
+  const int8_t *w;   // [n, k], row stride ldw
+  int64_t ldw;
+  const float *ws;   // [n]
+  float out_scale;
+  int8_t *out;       // [m, n], row stride ldo
+  int64_t ldo;
+  int64_t m, n, k;
+  int32_t *acc_out;  // optional [m, n] int32 accumulators (tests), may be null
+  uint32_t *status;
+};
+
+struct DeviceProps {
+  int sm_count = 0;
+  int smem_optin = 0;  // max dynamic shared memory per block
+  int cc_major = 0, cc_minor = 0;
+};
+const DeviceProps &device_props(int device);
+
+cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device);
+cudaError_t launch_i8(const I8Launch &a, cudaStream_t stream, int device);
+cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
+
+// Which kernel family launch_w4a8 / launch_i8 picked for a shape (tests and
+// benchmarks report it): 0 = generic per-element path, 1 = TMA-staged path.
+int w4a8_path(const W4A8Launch &a);
+int i8_path(const I8Launch &a);
+
+void set_last_error(const std::string &msg);
+
+}  // namespace ksb

@@ -1,0 +1,168 @@
+"""ctypes binding of libkernelsmith (B200).
+
+The product is the C library (ulir-kernels_b200/lib/libkernelsmith.so) and
+its headers (include/kernelsmith/*.h, include/ks_b200.h).  This module binds
+every exported symbol with its C signature so Python callers -- the tests,
+bench.py and the multi-GPU host logic -- go through exactly the entry points
+a C caller of the reference libkernelsmith would use.
+
+Buffers are passed as raw addresses: `addr(t)` accepts a torch tensor (device
+or host), a numpy array, an int or None.
+
+There is no Python or CPU implementation of any kernel here; if the library
+is missing, `lib()` raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_size_t, c_uint16, c_uint32, c_void_p
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent.parent
+LIB_PATH = PKG_DIR / "lib" / "libkernelsmith.so"
+
+KS_OK = 0
+KS_ERR_INVALID_ARG = -1
+KS_ERR_WORKSPACE = -2
+KS_ERR_UNSUPPORTED = -3
+KS_ERR_DEVICE = -4
+
+SCALE_F32 = 0
+SCALE_F16 = 1
+STATUS_WORDS = 2
+STATUS_BAD_SCALE = 0
+STATUS_TIMEOUT = 1
+
+_vp = c_void_p
+_sz = c_size_t
+_i32 = c_int32
+_f = c_float
+
+# name -> (restype, argtypes); the C declarations are in include/.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    # ks_common.h
+    "ks_target_name": (c_char_p, []),
+    "ks_simd_width_f32": (_sz, []),
+    # ks_quantized.h
+    "ks_dot_i8": (c_int, [_vp, _vp, _sz, _i32, _i32, _vp, _vp, _sz]),
+    "ks_matvec_i8": (c_int, [_vp, _vp, _sz, _vp, _sz, _sz, _i32, _i32, _vp, _sz]),
+    "ks_dot_w4a8": (c_int, [_vp, _vp, _vp, _sz, _sz, _f, _i32, _i32, _vp, _vp, _sz]),
+    "ks_matvec_w4a8": (
+        c_int,
+        [_vp, _vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _f, _i32, _i32, _vp, _sz],
+    ),
+    "ks_dot_i8_workspace": (_sz, [_sz]),
+    "ks_matvec_i8_workspace": (_sz, [_sz, _sz]),
+    "ks_dot_w4a8_workspace": (_sz, [_sz, _sz]),
+    "ks_matvec_w4a8_workspace": (_sz, [_sz, _sz, _sz]),
+    "ks_quantized_alignment": (_sz, []),
+    "ks_w4a8_packed_row_bytes": (_sz, [_sz]),
+    "ks_w4a8_scale_groups": (_sz, [_sz, _sz]),
+    # ks_b200.h
+    "ks_b200_version": (c_char_p, []),
+    "ks_b200_last_error": (c_char_p, []),
+    "ks_b200_device_count": (c_int, []),
+    "ks_b200_matvec_w4a8_f16": (
+        c_int,
+        [_vp, _vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _f, _i32, _i32],
+    ),
+    "ks_b200_matvec_i8_dequant": (c_int, [_vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _i32, _i32]),
+    "ks_b200_matvec_w4a8_async": (
+        c_int,
+        [_vp, _vp, _sz, _vp, c_int, _sz, _vp, _sz, _sz, _sz, _f, _i32, _i32, _vp, _vp],
+    ),
+    "ks_b200_matvec_i8_async": (c_int, [_vp, _vp, _sz, _vp, _sz, _sz, _i32, _i32, _vp]),
+    "ks_b200_matvec_i8_dequant_async": (
+        c_int,
+        [_vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _i32, _i32, _vp],
+    ),
+    "ks_b200_w4a8_kernel_path": (c_int, [_vp, _vp, _sz, _vp, c_int, _sz, _sz, _sz, _sz]),
+    "ks_b200_i8_kernel_path": (c_int, [_vp, _vp, _sz, _sz, _sz]),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+class KernelSmithError(RuntimeError):
+    def __init__(self, rc: int, msg: str):
+        super().__init__(f"libkernelsmith returned {rc}: {msg}")
+        self.rc = rc
+
+
+def lib() -> ctypes.CDLL:
+    """Load libkernelsmith (B200) once and bind every signature."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"libkernelsmith (B200) is not built at {LIB_PATH}; run "
+                "`python ulir-kernels_b200/build.py` (or __graft_entry__.build())"
+            )
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def addr(obj) -> int | None:
+    """Raw address of a torch tensor, numpy array, int or None."""
+    if obj is None:
+        return None
+    if isinstance(obj, int):
+        return obj
+    if hasattr(obj, "data_ptr"):
+        return obj.data_ptr()
+    if hasattr(obj, "ctypes"):
+        return obj.ctypes.data
+    raise TypeError(f"cannot take the address of {type(obj)!r}")
+
+
+def last_error() -> str:
+    return lib().ks_b200_last_error().decode()
+
+
+def check(rc: int) -> None:
+    if rc != KS_OK:
+        raise KernelSmithError(rc, last_error())
+
+
+def stream_handle(stream) -> int | None:
+    """cudaStream_t of a torch.cuda.Stream (None -> legacy default stream)."""
+    if stream is None:
+        return None
+    return int(stream.cuda_stream)
+
+
+def matvec_w4a8_async(x, w, w_stride, s, s_stride, y, rows, cols, group, sx, zx=0, zw=0,
+                      scale_type=SCALE_F16, status=None, stream=None) -> None:
+    """Queue one W4A8 GEMV on `stream` (device buffers); raises on a bad argument."""
+    check(
+        lib().ks_b200_matvec_w4a8_async(
+            addr(x), addr(w), w_stride, addr(s), scale_type, s_stride, addr(y), rows, cols,
+            group, sx, zx, zw, addr(status), stream_handle(stream),
+        )
+    )
+
+
+def matvec_i8_dequant_async(x, w, w_stride, ws, sa, y, rows, cols, zx=0, zw=0, stream=None) -> None:
+    check(
+        lib().ks_b200_matvec_i8_dequant_async(
+            addr(x), addr(w), w_stride, addr(ws), sa, addr(y), rows, cols, zx, zw,
+            stream_handle(stream),
+        )
+    )
+
+
+def matvec_i8_async(x, w, w_stride, y, rows, cols, zx=0, zw=0, stream=None) -> None:
+    check(
+        lib().ks_b200_matvec_i8_async(
+            addr(x), addr(w), w_stride, addr(y), rows, cols, zx, zw, stream_handle(stream)
+        )
+    )
+
+
+__all__ = [name for name in dir() if not name.startswith("_")]
