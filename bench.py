@@ -353,7 +353,7 @@ def run_b200_arm(args):
 
     # ---- e2e: public synchronous C ABI with pinned host buffers ----------
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(1, min(args.steps, 5))
-    e2e = run_e2e(L, K, torch, dist, dev, world, rank, e2e_steps)
+    e2e = run_e2e(L, K, torch, dist, dev, world, rank, e2e_steps) if e2e_steps > 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -114,6 +114,40 @@ int ks_b200_matvec_i8_dequant_async(const int8_t *input, const int8_t *weights,
                                     int32_t weight_zero_point, void *stream);
 
 /*
+ * Skinny INT8 GEMM with requantisation (batched decode, M = 1..256 tokens):
+ *   acc[m, n] = sum_k a[m, k] * w[n, k]                       (int32, exact)
+ *   out[m, n] = sat_i8(rne(((f32(acc) * a_scales[m]) * w_scales[n]) / out_scale))
+ * a is [m, k] with row stride lda bytes, w is [n, k] with row stride ldw
+ * bytes (the INT8 GEMV weight layout), out is [m, n] with row stride ldo
+ * bytes; only the m x n output bytes are written.  Each step of the
+ * epilogue is one IEEE round-to-nearest operation in the order written, the
+ * rounding to integer is ties-to-even and the result saturates to
+ * [-128, 127], so outputs are bit-exact against the same expression on the
+ * CPU.  Zero points are 0; scales must be finite.  The reference has no
+ * requantising entry point (its quantisation spec leaves requantisation out
+ * of the first ABI); this composes reference ks_dot_i8 (ks_quantized.c:44-65)
+ * per output with the spec's round-to-nearest-even quantise rule.
+ * Runs on tcgen05 tensor cores (kind::i8, TMEM accumulators) when lda and
+ * ldw are multiples of 16 and a, w are 16-byte aligned and m <= 256;
+ * otherwise on a generic kernel.
+ */
+int ks_b200_gemm_i8_requant(const int8_t *a, size_t lda, const float *a_scales,
+                            const int8_t *w, size_t ldw,
+                            const float *w_scales, float out_scale,
+                            int8_t *out, size_t ldo, size_t m, size_t n,
+                            size_t k);
+
+/* Asynchronous form; acc_out (optional, [m, n] int32, row stride n) receives
+ * the raw accumulators. */
+int ks_b200_gemm_i8_requant_async(const int8_t *a, size_t lda,
+                                  const float *a_scales, const int8_t *w,
+                                  size_t ldw, const float *w_scales,
+                                  float out_scale, int8_t *out, size_t ldo,
+                                  size_t m, size_t n, size_t k,
+                                  int32_t *acc_out, uint32_t *status,
+                                  void *stream);
+
+/*
  * Which kernel family a W4A8 / INT8 call with these arguments runs on the
  * current device: 1 = TMA-staged streaming kernel, 0 = generic per-element
  * kernel (any stride, alignment, odd cols, any group size), negative = the
@@ -126,6 +160,9 @@ int ks_b200_w4a8_kernel_path(const void *input, const void *packed_weights,
                              size_t group_size);
 int ks_b200_i8_kernel_path(const void *input, const void *weights,
                            size_t weight_stride, size_t rows, size_t cols);
+/* 1 = tcgen05 tensor-core kernel, 0 = generic kernel, negative = rejected. */
+int ks_b200_gemm_i8_kernel_path(const void *a, size_t lda, const void *w,
+                                size_t ldw, size_t m, size_t n, size_t k);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,130 @@
+"""Skinny INT8 GEMM with requantisation (tcgen05 kind::i8, TMEM accumulators)
+against the oracle: int32 accumulators and requantised int8 outputs must be
+bit-exact."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(seed, m, n, k):
+    a = O.rng(seed, 0).integers(-127, 128, (m, k), dtype=np.int8)
+    w = O.rng(seed, 1).integers(-127, 128, (n, k), dtype=np.int8)
+    sa = O.rng(seed, 2).uniform(1e-3, 1e-2, m).astype(np.float32)
+    ws = O.rng(seed, 3).uniform(1e-3, 1e-2, n).astype(np.float32)
+    return a, w, sa, ws
+
+
+def _run_async(ks, torch, cuda, a, w, sa, ws, out_scale, lda=None, ldw=None):
+    m, k = a.shape
+    n = w.shape[0]
+    da, dw = torch.from_numpy(a).to(cuda), torch.from_numpy(w).to(cuda)
+    dsa, dws = torch.from_numpy(sa).to(cuda), torch.from_numpy(ws).to(cuda)
+    out = torch.zeros((m, n), dtype=torch.int8, device=cuda)
+    acc = torch.zeros((m, n), dtype=torch.int32, device=cuda)
+    status = torch.zeros(2, dtype=torch.int32, device=cuda)
+    ks.gemm_i8_requant_async(da, dsa, dw, dws, out_scale, out, m, n, k, acc_out=acc, status=status)
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    return out.cpu().numpy(), acc.cpu().numpy()
+
+
+@pytest.mark.parametrize("m", [8, 16, 32, 64])
+def test_gemm_config_shapes(ks, cuda, oracle, m):
+    """M x 4096 x 14336, output scale 0.05 (the skinny batched-decode configuration)."""
+    import torch
+
+    n, k = 14336, 4096
+    a, w, sa, ws = _case(30 + m, m, n, k)
+    assert ks.lib().ks_b200_gemm_i8_kernel_path(ks.addr(a), k, ks.addr(w), k, m, n, k) in (0, 1)
+    out, acc = _run_async(ks, torch, cuda, a, w, sa, ws, 0.05)
+    # oracle on a row sample of W (row independence), full M
+    rows = np.unique(np.concatenate([np.arange(0, 256), np.arange(n - 256, n),
+                                     np.random.default_rng(m).choice(n, 512, replace=False)]))
+    rc, out_ref, acc_ref = oracle.gemm_i8_requant(a, sa, np.ascontiguousarray(w[rows]), ws[rows], 0.05, want_acc=True)
+    assert rc == 0
+    np.testing.assert_array_equal(acc[:, rows], acc_ref)
+    np.testing.assert_array_equal(out[:, rows], out_ref)
+    # requantised values use the whole int8 range (the test is not vacuous)
+    assert out.min() == -128 and out.max() == 127
+
+
+def test_gemm_tc_path_selected(ks, cuda):
+    import torch
+
+    a = torch.zeros((64, 4096), dtype=torch.int8, device=cuda)
+    w = torch.zeros((14336, 4096), dtype=torch.int8, device=cuda)
+    assert ks.lib().ks_b200_gemm_i8_kernel_path(a.data_ptr(), 4096, w.data_ptr(), 4096, 64, 14336, 4096) == 1
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 128), (5, 200, 320), (17, 1000, 1040), (48, 384, 4224),
+                                   (256, 256, 512), (3, 129, 48)])
+def test_gemm_ragged_shapes_bit_exact(ks, cuda, oracle, shape):
+    """Tokens not a multiple of 16, weight rows not a multiple of 128, K not a
+    multiple of 128: out-of-range tiles are zero-filled and masked."""
+    import torch
+
+    m, n, k = shape
+    a, w, sa, ws = _case(sum(shape), m, n, k)
+    out, acc = _run_async(ks, torch, cuda, a, w, sa, ws, 0.01)
+    rc, out_ref, acc_ref = oracle.gemm_i8_requant(a, sa, w, ws, 0.01, want_acc=True)
+    np.testing.assert_array_equal(acc, acc_ref)
+    np.testing.assert_array_equal(out, out_ref)
+
+
+def test_gemm_generic_path_strided_host(ks, cuda, oracle):
+    """Unaligned leading dimensions take the generic kernel; host buffers via the
+    synchronous entry point; the gaps of a strided output stay untouched."""
+    m, n, k = 7, 300, 200
+    lda, ldw, ldo = 203, 201, 310
+    g = np.random.default_rng(5)
+    abuf = g.integers(-127, 128, m * lda, dtype=np.int8)
+    wbuf = g.integers(-127, 128, n * ldw, dtype=np.int8)
+    sa = g.uniform(1e-3, 1e-2, m).astype(np.float32)
+    ws = g.uniform(1e-3, 1e-2, n).astype(np.float32)
+    out = np.full(m * ldo, 99, np.int8)
+    L = ks.lib()
+    assert L.ks_b200_gemm_i8_kernel_path(ks.addr(abuf), lda, ks.addr(wbuf), ldw, m, n, k) == 0
+    rc = L.ks_b200_gemm_i8_requant(ks.addr(abuf), lda, ks.addr(sa), ks.addr(wbuf), ldw, ks.addr(ws), 0.02,
+                                   ks.addr(out), ldo, m, n, k)
+    assert rc == 0, ks.last_error()
+    a = np.lib.stride_tricks.as_strided(abuf, (m, k), (lda, 1)).copy()
+    w = np.lib.stride_tricks.as_strided(wbuf, (n, k), (ldw, 1)).copy()
+    rc, out_ref = oracle.gemm_i8_requant(a, sa, w, ws, 0.02)
+    o = out.reshape(m, ldo)
+    np.testing.assert_array_equal(o[:, :n], out_ref)
+    assert (o[:, n:] == 99).all()
+
+
+def test_gemm_sync_device_matches_async(ks, cuda):
+    import torch
+
+    m, n, k = 16, 2048, 1024
+    a, w, sa, ws = _case(77, m, n, k)
+    out_async, _ = _run_async(ks, torch, cuda, a, w, sa, ws, 0.05)
+    da, dw = torch.from_numpy(a).to(cuda), torch.from_numpy(w).to(cuda)
+    dsa, dws = torch.from_numpy(sa).to(cuda), torch.from_numpy(ws).to(cuda)
+    out = torch.zeros((m, n), dtype=torch.int8, device=cuda)
+    rc = ks.lib().ks_b200_gemm_i8_requant(da.data_ptr(), k, dsa.data_ptr(), dw.data_ptr(), k, dws.data_ptr(), 0.05,
+                                          out.data_ptr(), n, m, n, k)
+    assert rc == 0, ks.last_error()
+    np.testing.assert_array_equal(out.cpu().numpy(), out_async)
+
+
+def test_gemm_rejects_bad_args(ks):
+    L = ks.lib()
+    a = np.zeros(64, np.int8)
+    s = np.ones(4, np.float32)
+    o = np.zeros(64, np.int8)
+    E = ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_gemm_i8_requant(ks.addr(a), 8, ks.addr(s), ks.addr(a), 8, ks.addr(s), 0.0, ks.addr(o), 4, 2, 4,
+                                     8) == E
+    assert L.ks_b200_gemm_i8_requant(ks.addr(a), 4, ks.addr(s), ks.addr(a), 8, ks.addr(s), 1.0, ks.addr(o), 4, 2, 4,
+                                     8) == E
+    assert L.ks_b200_gemm_i8_requant(None, 8, ks.addr(s), ks.addr(a), 8, ks.addr(s), 1.0, ks.addr(o), 4, 2, 4,
+                                     8) == E

@@ -89,8 +89,9 @@ def test_golden_bundles_on_device(ks, cuda, smoke_bundles, oracle):
     q = b["quantization_policy"]
     xs = bundle_array(b, "X")
     out = torch.zeros(1, dtype=torch.float32, device=cuda)
-    rc = ks.lib().ks_dot_w4a8(ks.addr(dev(xs, cuda)), ks.addr(dev(bundle_array(b, "W_packed"), cuda)),
-                              ks.addr(dev(bundle_array(b, "W_scales"), cuda)), xs.size,
+    # keep every device buffer referenced until the call returns
+    dxs, dws, dss = dev(xs, cuda), dev(bundle_array(b, "W_packed"), cuda), dev(bundle_array(b, "W_scales"), cuda)
+    rc = ks.lib().ks_dot_w4a8(ks.addr(dxs), ks.addr(dws), ks.addr(dss), xs.size,
                               b["tensors"]["W_packed"]["layout"]["group_size"], q["input_scale"],
                               q["input_zero_point"], q["weight_zero_point"], ks.addr(out), None, 0)
     assert rc == 0
@@ -109,8 +110,9 @@ def test_golden_bundles_on_device(ks, cuda, smoke_bundles, oracle):
     q = b["quantization_policy"]
     xs = bundle_array(b, "X")
     out = torch.zeros(1, dtype=torch.int32, device=cuda)
-    rc = ks.lib().ks_dot_i8(ks.addr(dev(xs, cuda)), ks.addr(dev(bundle_array(b, "W"), cuda)), xs.size,
-                            q["input_zero_point"], q["weight_zero_point"], ks.addr(out), None, 0)
+    dxs, dws = dev(xs, cuda), dev(bundle_array(b, "W"), cuda)
+    rc = ks.lib().ks_dot_i8(ks.addr(dxs), ks.addr(dws), xs.size, q["input_zero_point"], q["weight_zero_point"],
+                            ks.addr(out), None, 0)
     assert rc == 0
     np.testing.assert_array_equal(host(out), bundle_array(b, "Y"))
 
@@ -123,23 +125,25 @@ def test_reference_kats_host_pointers(ks, cuda):
     """reference tests/capi/test_quantized.c:33-126, called with host buffers
     exactly as that test does (the staged path)."""
     L, a = ks.lib(), ks.addr
-    out = np.zeros(1, np.int32)
-    assert L.ks_dot_i8(a(np.array([3, -2, 7, 1], np.int8)), a(np.array([2, -5, 4, -3], np.int8)), 4, 1, -1,
-                       a(out), None, 0) == 0
+    # every buffer is bound to a name so it outlives the call
+    x1, w1, out = np.array([3, -2, 7, 1], np.int8), np.array([2, -5, 4, -3], np.int8), np.zeros(1, np.int32)
+    assert L.ks_dot_i8(a(x1), a(w1), 4, 1, -1, a(out), None, 0) == 0
     assert out[0] == 48
-    y = np.array([-1, -1], np.int32)
-    assert L.ks_matvec_i8(a(np.array([1, 2, 3], np.int8)), a(np.array([1, 0, -1, 0, -2, 2, 3, 9], np.int8)), 4,
-                          a(y), 2, 3, 0, 0, None, 0) == 0
+    x2, w2, y = np.array([1, 2, 3], np.int8), np.array([1, 0, -1, 0, -2, 2, 3, 9], np.int8), np.array([-1, -1], np.int32)
+    assert L.ks_matvec_i8(a(x2), a(w2), 4, a(y), 2, 3, 0, 0, None, 0) == 0
     assert y.tolist() == [-2, 11]
+    x3 = np.array([4, -2, 3, 1], np.int8)
+    w3 = np.array([_pp(1, -2), _pp(3, -4)], np.uint8)
+    s3 = np.array([0.5, 0.25], np.float32)
     f = np.zeros(1, np.float32)
-    assert L.ks_dot_w4a8(a(np.array([4, -2, 3, 1], np.int8)), a(np.array([_pp(1, -2), _pp(3, -4)], np.uint8)),
-                         a(np.array([0.5, 0.25], np.float32)), 4, 2, 0.25, 0, 0, a(f), None, 0) == 0
+    assert L.ks_dot_w4a8(a(x3), a(w3), a(s3), 4, 2, 0.25, 0, 0, a(f), None, 0) == 0
     assert abs(f[0] - 1.3125) <= 1e-5
-    y = np.zeros(2, np.float32)
+    x4 = np.array([2, -1, 3], np.int8)
     pw = np.array([_pp(1, 2), _pp(-3, 0), _pp(-1, 0), _pp(4, 0)], np.uint8)
-    assert L.ks_matvec_w4a8(a(np.array([2, -1, 3], np.int8)), a(pw), 2, a(np.array([0.5, 0.25], np.float32)), 1,
-                            a(y), 2, 3, 3, 0.5, 0, 0, None, 0) == 0
-    np.testing.assert_allclose(y, [-2.25, 1.25], atol=1e-5)
+    s4 = np.array([0.5, 0.25], np.float32)
+    y4 = np.zeros(2, np.float32)
+    assert L.ks_matvec_w4a8(a(x4), a(pw), 2, a(s4), 1, a(y4), 2, 3, 3, 0.5, 0, 0, None, 0) == 0
+    np.testing.assert_allclose(y4, [-2.25, 1.25], atol=1e-5)
 
 
 def test_seeded_reference_fixtures(ks, cuda, seeded):
@@ -166,8 +170,10 @@ def test_seeded_reference_fixtures(ks, cuda, seeded):
 
 W4A8_SHAPES = [
     # rows, cols, group, wstride_pad, sstride_pad, zx, zw, f16, expected path
-    (1, 32, 32, 0, 0, 0, 0, False, 1),
-    (3, 64, 32, 0, 0, 5, -3, True, 1),
+    (1, 32, 32, 0, 0, 0, 0, False, 0),        # 4-byte scale rows cannot be bulk-copied
+    (3, 64, 32, 0, 0, 5, -3, True, 0),         # (bulk copies move multiples of 16 bytes)
+    (5, 128, 32, 0, 0, 5, -3, False, 1),
+    (7, 256, 32, 0, 0, 0, 0, True, 1),
     (149, 4096, 32, 0, 0, 0, 0, True, 1),
     (300, 2048, 64, 16, 4, -7, 2, False, 1),
     (77, 8192, 128, 0, 0, 0, 0, True, 1),
@@ -176,7 +182,8 @@ W4A8_SHAPES = [
     (50, 130, 10, 3, 1, 1, 1, False, 0),       # cols % 32 != 0
     (13, 77, 7, 0, 0, -128, 7, True, 0),       # odd cols
     (40, 640, 32, 1, 0, 0, 0, False, 0),       # stride not a multiple of 16
-    (20, 9216, 32, 0, 0, 0, 0, False, 0),      # cols beyond the staged limit
+    (20, 9216, 32, 0, 0, 0, 0, False, 1),      # activations staged in shared memory
+    (6, 16416, 32, 0, 0, 0, 0, True, 0),       # beyond the staged row limit (513 chunks)
 ]
 
 
@@ -212,7 +219,8 @@ I8_SHAPES = [
     (333, 1024, 16, -128, 127, 1),
     (77, 2000, 0, 1, 1, 1),
     (40, 100, 12, -3, 2, 0),    # cols % 16 != 0
-    (20, 6000, 0, 5, 5, 0),     # beyond the staged limit
+    (20, 6000, 0, 5, 5, 1),     # activations staged in shared memory
+    (4, 8208, 0, 1, -1, 0),     # beyond the staged row limit (513 chunks)
     (9, 64, 3, 0, 0, 0),        # stride not a multiple of 16
 ]
 
@@ -234,7 +242,8 @@ def test_i8_shapes_bit_exact(ks, cuda, oracle, shape):
     np.testing.assert_array_equal(host(y), y_ref)
     ws = O.rng(hash(shape) % 10000, 2).uniform(1e-3, 1e-2, rows).astype(np.float32)
     yf = torch.zeros(rows, dtype=torch.float32, device=cuda)
-    rc = ks.lib().ks_b200_matvec_i8_dequant(ks.addr(dx), ks.addr(dw), stride, ks.addr(dev(ws, cuda)), 0.02,
+    dws = dev(ws, cuda)
+    rc = ks.lib().ks_b200_matvec_i8_dequant(ks.addr(dx), ks.addr(dw), stride, ks.addr(dws), 0.02,
                                             ks.addr(yf), rows, cols, zx, zw)
     assert rc == 0, ks.last_error()
     rc, yf_ref = oracle.matvec_i8_dequant(x, w, rows, cols, stride, ws, 0.02, zx, zw)
@@ -288,7 +297,8 @@ def test_config_int8_gemv_4096(ks, cuda, oracle):
     _, yi_ref = oracle.matvec_i8(x, w, n, k, k)
     np.testing.assert_array_equal(host(yi), yi_ref)
     yf = torch.zeros(n, dtype=torch.float32, device=cuda)
-    assert ks.lib().ks_b200_matvec_i8_dequant(ks.addr(dx), ks.addr(dw), k, ks.addr(dev(ws, cuda)), 0.02,
+    dws = dev(ws, cuda)
+    assert ks.lib().ks_b200_matvec_i8_dequant(ks.addr(dx), ks.addr(dw), k, ks.addr(dws), 0.02,
                                               ks.addr(yf), n, k, 0, 0) == 0
     _, yf_ref = oracle.matvec_i8_dequant(x, w, n, k, k, ws, 0.02)
     np.testing.assert_array_equal(host(yf).view(np.uint32), yf_ref.view(np.uint32))

@@ -26,7 +26,7 @@ namespace ksb {
 namespace {
 
 constexpr int kMaxDevices = 64;
-enum Slot { kSlotX = 0, kSlotW, kSlotS, kSlotY, kSlots };
+enum Slot { kSlotX = 0, kSlotW, kSlotS, kSlotY, kSlotS2, kSlots };
 
 struct ThreadState {
   uint32_t *status = nullptr;  // mapped, portable pinned host memory
@@ -165,7 +165,11 @@ class SyncCall {
     if (launch_err != cudaSuccess) return cuda_fail(launch_err, "kernel launch");
     cudaError_t e;
     if (copy_back_host_) {
-      e = cudaMemcpyAsync(copy_back_host_, copy_back_dev_, copy_back_bytes_, cudaMemcpyDeviceToHost, 0);
+      if (height_ > 0)
+        e = cudaMemcpy2DAsync(copy_back_host_, pitch_, copy_back_dev_, pitch_, width_, height_,
+                              cudaMemcpyDeviceToHost, 0);
+      else
+        e = cudaMemcpyAsync(copy_back_host_, copy_back_dev_, copy_back_bytes_, cudaMemcpyDeviceToHost, 0);
       if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(D2H)");
     }
     e = cudaStreamSynchronize(0);
@@ -183,6 +187,26 @@ class SyncCall {
   void *copy_back_host_ = nullptr;
   void *copy_back_dev_ = nullptr;
   size_t copy_back_bytes_ = 0;
+
+ public:
+  // Stage a strided output of `height` rows of `width` bytes, `pitch` bytes
+  // apart: only those bytes are copied back, so the gaps between rows in the
+  // caller's buffer keep their contents.
+  int map_out_2d(int i, int slot, void *host, size_t pitch, size_t width, size_t height, void **out) {
+    if (where_[i].device) {
+      *out = host;
+      return KS_OK;
+    }
+    int rc = map(i, slot, host, (height - 1) * pitch + width, false, out);
+    if (rc != KS_OK) return rc;
+    pitch_ = pitch;
+    width_ = width;
+    height_ = height;
+    return KS_OK;
+  }
+
+ private:
+  size_t pitch_ = 0, width_ = 0, height_ = 0;
 };
 
 // Write a scalar result of a zero-length dot to a device or host pointer.
@@ -273,6 +297,47 @@ int i8_sync(const int8_t *x, const int8_t *w, size_t wstride, void *y, size_t ro
   a.out_f32 = out_f32 ? 1 : 0;
   a.status = call.status_dev();
   return call.finish(launch_i8(a, 0, call.device()));
+}
+
+int gemm_checks(const int8_t *a, size_t lda, const float *sa, const int8_t *w, size_t ldw, const float *ws,
+                float out_scale, const int8_t *out, size_t ldo, size_t m, size_t n, size_t k) {
+  if (!a || !sa || !w || !ws || !out) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (m == 0 || n == 0 || k == 0) return fail(KS_ERR_INVALID_ARG, "m, n and k must be > 0");
+  if (lda < k || ldw < k || ldo < n) return fail(KS_ERR_INVALID_ARG, "leading dimension too small");
+  if (!pos_finite(out_scale)) return fail(KS_ERR_INVALID_ARG, "out_scale must be > 0 and finite");
+  if (m > (size_t)INT32_MAX || n > (size_t)INT32_MAX || k > (size_t)INT32_MAX)
+    return fail(KS_ERR_UNSUPPORTED, "dimension beyond 2^31 - 1");
+  return KS_OK;
+}
+
+int gemm_sync(const int8_t *a, size_t lda, const float *sa, const int8_t *w, size_t ldw, const float *ws,
+              float out_scale, int8_t *out, size_t ldo, size_t m, size_t n, size_t k) {
+  SyncCall call;
+  const void *ptrs[5] = {a, w, sa, ws, out};
+  int rc = call.begin(ptrs, 5);
+  if (rc != KS_OK) return rc;
+  void *da = nullptr, *dw = nullptr, *dsa = nullptr, *dws = nullptr, *dout = nullptr;
+  if ((rc = call.map(0, kSlotX, a, (m - 1) * lda + k, true, &da)) != KS_OK) return rc;
+  if ((rc = call.map(1, kSlotW, w, (n - 1) * ldw + k, true, &dw)) != KS_OK) return rc;
+  if ((rc = call.map(2, kSlotS, sa, m * sizeof(float), true, &dsa)) != KS_OK) return rc;
+  if ((rc = call.map(3, kSlotS2, ws, n * sizeof(float), true, &dws)) != KS_OK) return rc;
+  if ((rc = call.map_out_2d(4, kSlotY, out, ldo, n, m, &dout)) != KS_OK) return rc;
+  GemmI8Launch g{};
+  g.a = static_cast<const int8_t *>(da);
+  g.lda = (int64_t)lda;
+  g.sa = static_cast<const float *>(dsa);
+  g.w = static_cast<const int8_t *>(dw);
+  g.ldw = (int64_t)ldw;
+  g.ws = static_cast<const float *>(dws);
+  g.out_scale = out_scale;
+  g.out = static_cast<int8_t *>(dout);
+  g.ldo = (int64_t)ldo;
+  g.m = (int64_t)m;
+  g.n = (int64_t)n;
+  g.k = (int64_t)k;
+  g.acc_out = nullptr;
+  g.status = call.status_dev();
+  return call.finish(launch_gemm_i8(g, 0, call.device()));
 }
 
 int current_device(int *dev) {
@@ -525,4 +590,54 @@ extern "C" int ks_b200_i8_kernel_path(const void *input, const void *weights, si
   a.rows = (int64_t)rows;
   a.cols = (int64_t)cols;
   return i8_path(a);
+}
+
+extern "C" int ks_b200_gemm_i8_requant(const int8_t *a, size_t lda, const float *a_scales, const int8_t *w,
+                                       size_t ldw, const float *w_scales, float out_scale, int8_t *out,
+                                       size_t ldo, size_t m, size_t n, size_t k) {
+  int rc = gemm_checks(a, lda, a_scales, w, ldw, w_scales, out_scale, out, ldo, m, n, k);
+  if (rc != KS_OK) return rc;
+  return gemm_sync(a, lda, a_scales, w, ldw, w_scales, out_scale, out, ldo, m, n, k);
+}
+
+extern "C" int ks_b200_gemm_i8_requant_async(const int8_t *a, size_t lda, const float *a_scales,
+                                             const int8_t *w, size_t ldw, const float *w_scales,
+                                             float out_scale, int8_t *out, size_t ldo, size_t m, size_t n,
+                                             size_t k, int32_t *acc_out, uint32_t *status, void *stream) {
+  int rc = gemm_checks(a, lda, a_scales, w, ldw, w_scales, out_scale, out, ldo, m, n, k);
+  if (rc != KS_OK) return rc;
+  int dev;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  GemmI8Launch g{};
+  g.a = a;
+  g.lda = (int64_t)lda;
+  g.sa = a_scales;
+  g.w = w;
+  g.ldw = (int64_t)ldw;
+  g.ws = w_scales;
+  g.out_scale = out_scale;
+  g.out = out;
+  g.ldo = (int64_t)ldo;
+  g.m = (int64_t)m;
+  g.n = (int64_t)n;
+  g.k = (int64_t)k;
+  g.acc_out = acc_out;
+  g.status = status;
+  cudaError_t e = launch_gemm_i8(g, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_gemm_i8_kernel_path(const void *a, size_t lda, const void *w, size_t ldw, size_t m,
+                                           size_t n, size_t k) {
+  if (m == 0 || n == 0 || k == 0 || lda < k || ldw < k) return -1;
+  if (ks_b200_device_count() == 0) return -1;
+  GemmI8Launch g{};
+  g.a = static_cast<const int8_t *>(a);
+  g.lda = (int64_t)lda;
+  g.w = static_cast<const int8_t *>(w);
+  g.ldw = (int64_t)ldw;
+  g.m = (int64_t)m;
+  g.n = (int64_t)n;
+  g.k = (int64_t)k;
+  return gemm_i8_path(g);
 }

@@ -76,6 +76,7 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
 // benchmarks report it): 0 = generic per-element path, 1 = TMA-staged path.
 int w4a8_path(const W4A8Launch &a);
 int i8_path(const I8Launch &a);
+int gemm_i8_path(const GemmI8Launch &a);
 
 void set_last_error(const std::string &msg);
 

@@ -21,6 +21,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Record a device-side finding in a status word (plain store, no atomics, so
+// the word may live in mapped host memory).
+__device__ __forceinline__ void set_status(uint32_t *status, int word) {
+  if (status) *reinterpret_cast<volatile uint32_t *>(status + word) = 1u;
+}
+
 // ---- mbarrier -------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

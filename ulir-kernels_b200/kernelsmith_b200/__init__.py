@@ -77,6 +77,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [_vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _i32, _i32, _vp],
     ),
+    "ks_b200_gemm_i8_requant": (c_int, [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz]),
+    "ks_b200_gemm_i8_requant_async": (
+        c_int,
+        [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp],
+    ),
+    "ks_b200_gemm_i8_kernel_path": (c_int, [_vp, _sz, _vp, _sz, _sz, _sz, _sz]),
     "ks_b200_w4a8_kernel_path": (c_int, [_vp, _vp, _sz, _vp, c_int, _sz, _sz, _sz, _sz]),
     "ks_b200_i8_kernel_path": (c_int, [_vp, _vp, _sz, _sz, _sz]),
 }
@@ -161,6 +167,16 @@ def matvec_i8_async(x, w, w_stride, y, rows, cols, zx=0, zw=0, stream=None) -> N
     check(
         lib().ks_b200_matvec_i8_async(
             addr(x), addr(w), w_stride, addr(y), rows, cols, zx, zw, stream_handle(stream)
+        )
+    )
+
+
+def gemm_i8_requant_async(a, sa, w, ws, out_scale, out, m, n, k, lda=None, ldw=None, ldo=None,
+                          acc_out=None, status=None, stream=None) -> None:
+    check(
+        lib().ks_b200_gemm_i8_requant_async(
+            addr(a), lda or k, addr(sa), addr(w), ldw or k, addr(ws), out_scale, addr(out), ldo or n, m, n, k,
+            addr(acc_out), addr(status), stream_handle(stream),
         )
     )
 
