@@ -291,10 +291,17 @@ def run_b200_arm(args):
     per_chunk = MATS // CHUNKS
 
     def gemv_chunk(c):
-        for j in range(per_chunk):
-            m = c * per_chunk + j
-            K.matvec_w4a8_async(X[m], W[m], COLS // 2, S[m], COLS // GROUP, Yloc[c, j], ROWS, COLS, GROUP, SX,
-                                scale_type=K.SCALE_F16, status=status, stream=main)
+        # one batched launch: 16 independent GEMVs streamed back to back
+        ms = range(c * per_chunk, (c + 1) * per_chunk)
+        K.matvec_w4a8_batch_async([X[m] for m in ms], [W[m] for m in ms], [S[m] for m in ms],
+                                  [Yloc[c, j] for j in range(per_chunk)], COLS // 2, COLS // GROUP, ROWS, COLS,
+                                  GROUP, SX, scale_type=K.SCALE_F16, status=status, stream=main)
+
+    def gemv_single_chain():
+        # the same 64 GEMVs as 64 single launches (programmatic dependent launch chain)
+        for m in range(MATS):
+            K.matvec_w4a8_async(X[m], W[m], COLS // 2, S[m], COLS // GROUP, Yloc[m // per_chunk, m % per_chunk],
+                                ROWS, COLS, GROUP, SX, scale_type=K.SCALE_F16, status=status, stream=main)
 
     # one CUDA graph per chunk of 16 GEMVs (launch-bound inner loop)
     graphs = []
@@ -345,9 +352,30 @@ def run_b200_arm(args):
     st = status.cpu().tolist()
     assert st == [0, 0], f"device status {st}"
 
+    # secondary: the single-GEMV launch chain (what a dependent decode chain of
+    # ks_* calls costs per GEMV), timed the same way on this rank
+    chain = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(main):
+        gemv_single_chain()
+    main.synchronize()
+    with torch.cuda.graph(chain, stream=main):
+        gemv_single_chain()
+    with torch.cuda.stream(main):
+        for _ in range(3):
+            chain.replay()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(main)
+        n_chain = max(3, min(args.steps, 50))
+        for _ in range(n_chain):
+            chain.replay()
+        c1.record(main)
+        c1.synchronize()
+    chain_us = c0.elapsed_time(c1) * 1e3 / (n_chain * MATS)
+    del chain
+
     total_bytes = gemv_bytes() * MATS * args.steps * world
     value = total_bytes / (ms * 1e-3) / 1e12
-    per_launch_s = ms * 1e-3 / (MATS * args.steps)
+    per_launch_s = ms * 1e-3 / (MATS * args.steps)  # per GEMV
     peak, peak_kind = measured_hbm_peak()
     achieved = gemv_bytes() / per_launch_s / 1e9
 
@@ -376,11 +404,15 @@ def run_b200_arm(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                         "kernel": "gemv_stream_kernel<W4A8Op<__half,4>>",
-                         "bytes_per_launch": gemv_bytes(), "launch_us": per_launch_s * 1e6},
+                         "kernel": "gemv_stream_kernel<W4A8Op<__half,4,false>,16> (batched, 16 GEMVs per launch)",
+                         "bytes_per_gemv": gemv_bytes(), "us_per_gemv": per_launch_s * 1e6,
+                         "gemvs_per_launch": MATS // CHUNKS},
+            "single_launch_chain": {"us_per_gemv": chain_us, "GB_s": gemv_bytes() / chain_us / 1e3,
+                                    "frac": gemv_bytes() / chain_us / 1e3 / peak,
+                                    "note": "64 single-GEMV launches, PDL chain, per GPU"},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": MATS * args.steps * world,
+            "gpu_launches": CHUNKS * args.steps * world,
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)

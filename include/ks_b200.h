@@ -114,6 +114,43 @@ int ks_b200_matvec_i8_dequant_async(const int8_t *input, const int8_t *weights,
                                     int32_t weight_zero_point, void *stream);
 
 /*
+ * A batch of independent GEMVs of one shape in one launch: matrix i computes
+ * outputs[i] from inputs[i], packed_weights[i] and weight_scales[i] exactly
+ * as ks_b200_matvec_w4a8_async would (bitwise the same results), but every SM
+ * streams its rows of all the matrices back to back through one deep shared-
+ * memory ring, so there is no gap between matrices.  For projections that
+ * share a shape and run together (Q/K/V or gate/up of a decode step, the
+ * experts of a mixture-of-experts layer, the layers of a batch of
+ * independent requests).  The pointer arrays are host memory with `count`
+ * entries; the buffers they point to are device memory.  Argument checks are
+ * ks_matvec_w4a8's, per matrix.  Batches beyond 64 matrices are split into
+ * launches of at most 64.
+ */
+int ks_b200_matvec_w4a8_batch_async(int count, const int8_t *const *inputs,
+                                    const uint8_t *const *packed_weights,
+                                    const void *const *weight_scales,
+                                    float *const *outputs,
+                                    size_t packed_stride_bytes, int scale_type,
+                                    size_t scale_stride, size_t rows,
+                                    size_t cols, size_t group_size,
+                                    float input_scale,
+                                    int32_t input_zero_point,
+                                    int32_t weight_zero_point,
+                                    uint32_t *status, void *stream);
+
+/* INT8 batch: int32 outputs (ks_matvec_i8) when weight_scales is NULL,
+ * else f32 outputs with the per-channel dequant epilogue of
+ * ks_b200_matvec_i8_dequant (outputs are float* then). */
+int ks_b200_matvec_i8_batch_async(int count, const int8_t *const *inputs,
+                                  const int8_t *const *weights,
+                                  const float *const *weight_scales,
+                                  void *const *outputs, size_t weight_stride,
+                                  size_t rows, size_t cols,
+                                  int32_t input_zero_point,
+                                  int32_t weight_zero_point, float input_scale,
+                                  void *stream);
+
+/*
  * Skinny INT8 GEMM with requantisation (batched decode, M = 1..256 tokens):
  *   acc[m, n] = sum_k a[m, k] * w[n, k]                       (int32, exact)
  *   out[m, n] = sat_i8(rne(((f32(acc) * a_scales[m]) * w_scales[n]) / out_scale))

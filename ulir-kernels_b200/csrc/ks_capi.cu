@@ -641,3 +641,71 @@ extern "C" int ks_b200_gemm_i8_kernel_path(const void *a, size_t lda, const void
   g.k = (int64_t)k;
   return gemm_i8_path(g);
 }
+
+// ===================================================== batched (grouped) GEMV
+extern "C" int ks_b200_matvec_w4a8_batch_async(int count, const int8_t *const *inputs,
+                                               const uint8_t *const *packed_weights,
+                                               const void *const *weight_scales, float *const *outputs,
+                                               size_t packed_stride_bytes, int scale_type, size_t scale_stride,
+                                               size_t rows, size_t cols, size_t group_size, float input_scale,
+                                               int32_t input_zero_point, int32_t weight_zero_point,
+                                               uint32_t *status, void *stream) {
+  if (count < 0 || (count > 0 && (!inputs || !packed_weights || !weight_scales || !outputs)))
+    return fail(KS_ERR_INVALID_ARG, "bad batch arrays");
+  if (scale_type != kScaleF32 && scale_type != kScaleF16) return fail(KS_ERR_INVALID_ARG, "unknown scale_type");
+  for (int i = 0; i < count; ++i) {
+    int rc = w4a8_matvec_checks(inputs[i], packed_weights[i], packed_stride_bytes, weight_scales[i],
+                                scale_stride, outputs[i], rows, cols, group_size, input_scale, input_zero_point,
+                                weight_zero_point);
+    if (rc != KS_OK) return rc;
+  }
+  if (count == 0) return KS_OK;
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  W4A8Launch a{};
+  a.wstride = (int64_t)packed_stride_bytes;
+  a.sstride = (int64_t)scale_stride;
+  a.stype = scale_type;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group_size;
+  a.sx = input_scale;
+  a.zx = input_zero_point;
+  a.zw = weight_zero_point;
+  a.status = status;
+  GemvBatch b{count, inputs, reinterpret_cast<const void *const *>(packed_weights), weight_scales,
+              reinterpret_cast<void *const *>(outputs)};
+  cudaError_t e = launch_w4a8_batch(a, b, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_matvec_i8_batch_async(int count, const int8_t *const *inputs,
+                                             const int8_t *const *weights, const float *const *weight_scales,
+                                             void *const *outputs, size_t weight_stride, size_t rows, size_t cols,
+                                             int32_t input_zero_point, int32_t weight_zero_point,
+                                             float input_scale, void *stream) {
+  if (count < 0 || (count > 0 && (!inputs || !weights || !outputs)))
+    return fail(KS_ERR_INVALID_ARG, "bad batch arrays");
+  if (rows == 0 || cols == 0 || weight_stride < cols)
+    return fail(KS_ERR_INVALID_ARG, "rows/cols must be > 0 and weight_stride >= cols");
+  if (!i8_zp_ok(input_zero_point) || !i8_zp_ok(weight_zero_point))
+    return fail(KS_ERR_INVALID_ARG, "zero point out of range");
+  for (int i = 0; i < count; ++i)
+    if (!inputs[i] || !weights[i] || !outputs[i] || (weight_scales && !weight_scales[i]))
+      return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (count == 0) return KS_OK;
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  I8Launch a{};
+  a.wstride = (int64_t)weight_stride;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.zx = input_zero_point;
+  a.zw = weight_zero_point;
+  a.sa = input_scale;
+  a.out_f32 = weight_scales ? 1 : 0;
+  GemvBatch b{count, inputs, reinterpret_cast<const void *const *>(weights),
+              reinterpret_cast<const void *const *>(weight_scales), outputs};
+  cudaError_t e = launch_i8_batch(a, b, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}

@@ -2,18 +2,22 @@
 //
 // Two kernel families per operation:
 //
-//  * gemv_stream_kernel<Op>: the HBM-streaming path.  One CTA per SM owns a
-//    contiguous block of rows.  A producer warp streams the block's weight
-//    rows (and their scale rows) into a ring of shared-memory stages with
-//    cp.async.bulk (the TMA engine, 1-D bulk form, no tensor map, no
-//    multicast), one mbarrier per stage.  Eight consumer warps take pairs of
-//    rows, unpack int4 with LOP3, multiply with dp4a and reduce each row with
-//    warp shuffles in a fixed order, so results are bitwise reproducible.
-//    A CTA uses at most ~108 KB of shared memory and 288 threads, so two CTAs
-//    fit on an SM: with programmatic dependent launch the next GEMV on the
-//    stream starts streaming its weights while the current one finishes, and
-//    only waits for the previous kernel (griddepcontrol.wait) before it reads
-//    the activation vector or writes its output.
+//  * gemv_stream_kernel<Op, CW>: the HBM-streaming path.  One CTA per SM
+//    owns a contiguous block of rows of every matrix of a batch (a single
+//    GEMV is a batch of one).  A producer warp streams those rows -- the
+//    weights and their scale rows, matrix after matrix -- into a ring of
+//    shared-memory stages with cp.async.bulk (the TMA engine, 1-D bulk form,
+//    no tensor map, no multicast), one mbarrier per stage.  CW consumer warps
+//    take pairs of rows, unpack int4 with LOP3, multiply with dp4a and reduce
+//    each row with warp shuffles in a fixed order, so results are bitwise
+//    reproducible.  Each matrix's activation vector is prepared once per CTA
+//    into a double-buffered shared-memory slot (the next one while the current
+//    matrix is computed), so the ring never drains between matrices.
+//      - single GEMV: CW = 8, at most ~108 KB of shared memory, two CTAs per
+//        SM.  With programmatic dependent launch the next GEMV on the stream
+//        starts streaming its weights while this one finishes and waits for
+//        it (griddepcontrol.wait) only before reading x or writing y.
+//      - batch: CW = 16, one CTA per SM with a deep ring (~220 KB).
 //  * *_generic_kernel: a warp-per-row, byte-load path for any stride,
 //    alignment, odd column count or group size.  Same contract, slower.
 //
@@ -48,30 +52,39 @@
 
 namespace ksb {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kStreamThreads = (kConsumerWarps + 1) * 32;
 constexpr int kMaxStages = 16;
-constexpr int kBarBytes = 1024;  // barrier area at the start of shared memory
-// Shared memory per CTA: two CTAs must fit in the SM's 228 KB (1 KB of each
-// CTA is reserved by the hardware).
-constexpr int kSmemPerCta = 108 * 1024;
+constexpr int kBarBytes = 1024;      // barrier area at the start of shared memory
+constexpr int kMaxItems = 64;        // matrices per launch
+constexpr int kSmemSingle = 108 * 1024;  // two CTAs per SM (228 KB, 1 KB reserved each)
+constexpr int kSmemBatch = 220 * 1024;   // one CTA per SM
+constexpr int kMaxStreamChunks = 512;    // W4A8 rows up to 16384 columns, INT8 up to 8192
 
-// Geometry of the streamed weight block, shared by all stream kernels.
+struct GemvItem {
+  const int8_t *x;
+  const uint8_t *w;
+  const uint8_t *s;  // scales (W4A8) or per-channel dequant scales (INT8 f32 out)
+  void *y;
+};
+struct GemvItems {
+  GemvItem it[kMaxItems];
+};
+
+// Geometry of the streamed weight blocks, shared by all stream kernels.
 struct StreamGeom {
-  const uint8_t *w;     // first weight row
   int64_t wstride;      // bytes between weight rows
-  const uint8_t *s;     // first side row (scales) or null
   int64_t sstride;      // bytes between side rows
   int64_t rows;
+  int32_t count;        // matrices in this launch
   int32_t n_cta;
   int32_t rps;          // rows per stage (even)
   int32_t nst;          // stages in the ring
   int32_t row_bytes;    // streamed bytes per weight row
   int32_t srow_bytes;   // streamed bytes per side row (0: none)
   int32_t stage_bytes;
-  int32_t x_bytes;      // shared-memory activation area (0: activations in registers)
+  int32_t xbuf_bytes;   // one prepared-activation buffer
   int32_t w_contig;     // wstride == row_bytes: one copy per stage
   int32_t s_contig;
+  int32_t x_al16;       // every activation vector 16-byte aligned
   uint32_t *status;
 };
 
@@ -99,8 +112,10 @@ struct ScaleBits<float> {
   static constexpr int kBytes = 4;
   __device__ __forceinline__ static uint32_t load(const uint8_t *p) { return lds_u32(p); }
   __device__ __forceinline__ static uint32_t gload(const float *p) { return __float_as_uint(__ldg(p)); }
-  // 0 < bits < +inf; negative values, zero, inf and nan fail
-  __device__ __forceinline__ static bool bad(uint32_t b) { return (b - 1u) >= 0x7F7FFFFFu; }
+  // 0 < bits < +inf; negative values, zero, inf and nan fail.  Kernels
+  // keep max(bits - 1) over the scales they read and test it once.
+  static constexpr uint32_t kBadFrom = 0x7F7FFFFFu;
+  __device__ __forceinline__ static bool bad(uint32_t b) { return (b - 1u) >= kBadFrom; }
   __device__ __forceinline__ static float f32(uint32_t b) { return __uint_as_float(b); }
 };
 template <>
@@ -110,7 +125,8 @@ struct ScaleBits<__half> {
   __device__ __forceinline__ static uint32_t gload(const __half *p) {
     return __half_as_ushort(__ldg(p));
   }
-  __device__ __forceinline__ static bool bad(uint32_t b) { return (b - 1u) >= 0x7BFFu; }
+  static constexpr uint32_t kBadFrom = 0x7BFFu;
+  __device__ __forceinline__ static bool bad(uint32_t b) { return (b - 1u) >= kBadFrom; }
   __device__ __forceinline__ static float f32(uint32_t b) {
     return __half2float(__ushort_as_half((unsigned short)b));
   }
@@ -122,15 +138,33 @@ __device__ __forceinline__ float warp_sum_f32(float v) {
   return v;
 }
 
-__device__ __forceinline__ void load_bytes(const int8_t *p, bool al16, uint32_t *X, int words) {
+// Two partial sums of the same warp reduced together: after the first
+// exchange lanes 0-15 hold a's partials and lanes 16-31 b's, so the rest of
+// the butterfly carries one value.  Lane 0 ends with sum(a), lane 16 with
+// sum(b).  Fixed order: bitwise reproducible.
+template <typename T>
+__device__ __forceinline__ T warp_sum_pair(T a, T b, int lane) {
+  const bool upper = (lane & 16) != 0;
+  T keep = upper ? b : a;
+  const T give = upper ? a : b;
+  keep += __shfl_xor_sync(0xffffffffu, give, 16);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+  return keep;
+}
+
+template <int WORDS>
+__device__ __forceinline__ void load_words(const int8_t *p, bool al16, uint32_t (&X)[WORDS]) {
   if (al16) {
-    for (int i = 0; i < words; i += 4) {
+#pragma unroll
+    for (int i = 0; i < WORDS; i += 4) {
       const uint4 a = __ldg(reinterpret_cast<const uint4 *>(p) + i / 4);
       X[i] = a.x; X[i + 1] = a.y; X[i + 2] = a.z; X[i + 3] = a.w;
     }
   } else {
     const uint8_t *q = reinterpret_cast<const uint8_t *>(p);
-    for (int i = 0; i < words; ++i)
+#pragma unroll
+    for (int i = 0; i < WORDS; ++i)
       X[i] = (uint32_t)q[4 * i] | ((uint32_t)q[4 * i + 1] << 8) | ((uint32_t)q[4 * i + 2] << 16) |
              ((uint32_t)q[4 * i + 3] << 24);
   }
@@ -138,44 +172,26 @@ __device__ __forceinline__ void load_bytes(const int8_t *p, bool al16, uint32_t 
 
 // ---------------------------------------------------------------- W4A8 op --
 struct W4A8OpParams {
-  const int8_t *x;
-  float *y;
   int32_t chunks;  // 32-element chunks per row (cols / 32)
   int32_t gshift;  // log2(group / 32)
   float sx;
   int32_t zx, zw;
-  int32_t x_al16;
 };
 
-// Per chunk of 32 activations: the even-k and odd-k bytes of each packed
-// word, and kc = (8 + zw) * sum(x - zx) over the chunk.
-__device__ __forceinline__ void w4a8_prep_chunk(const W4A8OpParams &p, int c, uint32_t (&xe)[4],
-                                                uint32_t (&xo)[4], int &kc) {
-  uint32_t X[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (c < p.chunks) load_bytes(p.x + 32 * c, p.x_al16 != 0, X, 8);
-  int sumx = 0;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    xe[q] = prmt(X[2 * q], X[2 * q + 1], 0x6420);
-    xo[q] = prmt(X[2 * q], X[2 * q + 1], 0x7531);
-    sumx = dp4a_ss(X[2 * q], 0x01010101u, sumx);
-    sumx = dp4a_ss(X[2 * q + 1], 0x01010101u, sumx);
-  }
-  kc = (8 + p.zw) * (sumx - 32 * p.zx);
-}
-
 // int32 dot of one 32-element chunk (packed word v) against prepared x.
-__device__ __forceinline__ int w4a8_chunk_dot(const uint4 v, const uint32_t (&xe)[4], const uint32_t (&xo)[4],
-                                              int kc, int zx) {
+template <bool ZX>
+__device__ __forceinline__ int w4a8_chunk_dot(const uint4 v, const uint4 xe, const uint4 xo, int kc, int zx) {
   const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+  const uint32_t e[4] = {xe.x, xe.y, xe.z, xe.w};
+  const uint32_t o[4] = {xo.x, xo.y, xo.z, xo.w};
   int lo = 0, hi = 0;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    lo = dp4a_us(and_xor(vw[q], 0x0F0F0F0Fu, 0x08080808u), xe[q], lo);
-    hi = dp4a_us(and_xor(vw[q], 0xF0F0F0F0u, 0x80808080u), xo[q], hi);
+    lo = dp4a_us(and_xor(vw[q], 0x0F0F0F0Fu, 0x08080808u), e[q], lo);
+    hi = dp4a_us(and_xor(vw[q], 0xF0F0F0F0u, 0x80808080u), o[q], hi);
   }
   int acc = lo + (hi >> 4) - kc;
-  if (zx != 0) {
+  if (ZX) {
     uint32_t su = 0, sh = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -187,170 +203,147 @@ __device__ __forceinline__ int w4a8_chunk_dot(const uint4 v, const uint32_t (&xe
   return acc;
 }
 
-// XS: activations staged in shared memory (long rows) instead of registers.
-template <typename ST, int NCPL, bool XS>
+// Prepared activations, per 32-element chunk c: at xb + 32c the even-k bytes
+// of the chunk's four packed words, at xb + 32c + 16 the odd-k bytes, and at
+// xb + 32*chunks + 4c the constant kc = (8 + zw) * sum(x - zx).
+// ZX: input zero point != 0.
+template <typename ST, int NCPL, bool ZX>
 struct W4A8Op {
   using Params = W4A8OpParams;
   using SB = ScaleBits<ST>;
-  struct Lane {
-    uint32_t xe[XS ? 1 : NCPL][4];
-    uint32_t xo[XS ? 1 : NCPL][4];
-    int kc[XS ? 1 : NCPL];
-  };
+  static constexpr int kRawWords = 8;  // 32 activation bytes per chunk
+  struct Lane {};
 
-  // Called by every consumer thread after griddepcontrol.wait.
-  __device__ __forceinline__ static void init(const Params &p, Lane &L, int lane, uint8_t *xs, int ctid) {
-    if (XS) {
-      for (int c = ctid; c < p.chunks; c += kConsumerWarps * 32) {
-        uint32_t xe[4], xo[4];
-        int kc;
-        w4a8_prep_chunk(p, c, xe, xo, kc);
-        uint4 *d = reinterpret_cast<uint4 *>(xs + 32 * c);
-        d[0] = make_uint4(xe[0], xe[1], xe[2], xe[3]);
-        d[1] = make_uint4(xo[0], xo[1], xo[2], xo[3]);
-        reinterpret_cast<int *>(xs + 32 * p.chunks)[c] = kc;
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-    } else {
-#pragma unroll
-      for (int j = 0; j < NCPL; ++j) w4a8_prep_chunk(p, lane + 32 * j, L.xe[j], L.xo[j], L.kc[j]);
-    }
+  static int xbuf_bytes(int chunks) { return ((chunks * 36 + 127) / 128) * 128; }
+
+  __device__ __forceinline__ static void load_raw(const int8_t *x, int c, bool al16, uint32_t (&raw)[8]) {
+    load_words<8>(x + 32 * c, al16, raw);
   }
 
+  __device__ __forceinline__ static void store_prep(const Params &p, const uint32_t (&X)[8], int c, uint8_t *xb) {
+    uint32_t e[4], o[4];
+    int sumx = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      e[q] = prmt(X[2 * q], X[2 * q + 1], 0x6420);
+      o[q] = prmt(X[2 * q], X[2 * q + 1], 0x7531);
+      sumx = dp4a_ss(X[2 * q], 0x01010101u, sumx);
+      sumx = dp4a_ss(X[2 * q + 1], 0x01010101u, sumx);
+    }
+    uint4 *d = reinterpret_cast<uint4 *>(xb + 32 * c);
+    d[0] = make_uint4(e[0], e[1], e[2], e[3]);
+    d[1] = make_uint4(o[0], o[1], o[2], o[3]);
+    reinterpret_cast<int *>(xb + 32 * p.chunks)[c] = (8 + p.zw) * (sumx - 32 * p.zx);
+  }
+
+  __device__ __forceinline__ static void lane_init(const Params &, Lane &, const uint8_t *, int) {}
+
   // Two rows (b valid if has_b) whose weights and scale rows are in shared
-  // memory -> y.  Returns true if a scale of a processed row is invalid.
-  __device__ __forceinline__ static bool rows2(const Params &p, const Lane &L, const uint8_t *xs,
-                                               const uint8_t *wa, const uint8_t *sa, const uint8_t *wb,
-                                               const uint8_t *sb, int64_t ga, bool has_b, int lane) {
+  // memory -> y.  Returns max(scale bits - 1) over the scales read.
+  __device__ __forceinline__ static uint32_t rows2(const Params &p, const Lane &, const uint8_t *xb,
+                                                   const uint8_t *wa, const uint8_t *sa, const uint8_t *wb,
+                                                   const uint8_t *sb, const GemvItem &it, int64_t ga, bool has_b,
+                                                   int lane) {
     float pa = 0.0f, pb = 0.0f;
-    uint32_t bad = 0;
+    uint32_t mx = 0;
 #pragma unroll
     for (int j = 0; j < NCPL; ++j) {
       const int c = lane + 32 * j;
       if (c < p.chunks) {
-        uint32_t xe[4], xo[4];
-        int kc;
-        if (XS) {
-          const uint4 e = lds128(xs + 32 * c), o = lds128(xs + 32 * c + 16);
-          xe[0] = e.x; xe[1] = e.y; xe[2] = e.z; xe[3] = e.w;
-          xo[0] = o.x; xo[1] = o.y; xo[2] = o.z; xo[3] = o.w;
-          kc = (int)lds_u32(xs + 32 * p.chunks + 4 * c);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            xe[q] = L.xe[XS ? 0 : j][q];
-            xo[q] = L.xo[XS ? 0 : j][q];
-          }
-          kc = L.kc[XS ? 0 : j];
-        }
+        const uint4 xe = lds128(xb + 32 * c);
+        const uint4 xo = lds128(xb + 32 * c + 16);
+        const int kc = (int)lds_u32(xb + 32 * p.chunks + 4 * c);
         const int g = c >> p.gshift;
         const uint4 va = lds128(wa + 16 * c);
         const uint4 vb = lds128(wb + 16 * c);
         const uint32_t ba = SB::load(sa + g * SB::kBytes);
-        const uint32_t bb = SB::load(sb + g * SB::kBytes);
-        const int acc_a = w4a8_chunk_dot(va, xe, xo, kc, p.zx);
-        const int acc_b = w4a8_chunk_dot(vb, xe, xo, kc, p.zx);
-        bad |= (uint32_t)SB::bad(ba) | ((uint32_t)SB::bad(bb) & (uint32_t)has_b);
+        const uint32_t bb = has_b ? SB::load(sb + g * SB::kBytes) : 1u;
+        const int acc_a = w4a8_chunk_dot<ZX>(va, xe, xo, kc, p.zx);
+        const int acc_b = w4a8_chunk_dot<ZX>(vb, xe, xo, kc, p.zx);
+        mx = max(mx, max(ba - 1u, bb - 1u));
         pa = fmaf((float)acc_a, SB::f32(ba), pa);
         pb = fmaf((float)acc_b, SB::f32(bb), pb);
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      pa += __shfl_xor_sync(0xffffffffu, pa, o);
-      pb += __shfl_xor_sync(0xffffffffu, pb, o);
-    }
-    if (lane == 0) p.y[ga] = pa * p.sx;
-    if (lane == 1 && has_b) p.y[ga + 1] = pb * p.sx;
-    return bad != 0;
+    const float t = warp_sum_pair(pa, pb, lane);
+    float *y = reinterpret_cast<float *>(it.y);
+    if (lane == 0) y[ga] = t * p.sx;
+    if (lane == 16 && has_b) y[ga + 1] = t * p.sx;
+    return mx;
   }
+
+  __device__ __forceinline__ static bool bad(uint32_t mx) { return mx >= SB::kBadFrom; }
 };
 
 // ---------------------------------------------------------------- INT8 op --
 struct I8OpParams {
-  const int8_t *x;
-  void *y;
-  const float *ws;
   float sa;
   int32_t chunks;  // 16-element chunks per row (cols / 16)
   int32_t zx, zw;
-  int32_t x_al16;
 };
 
-template <int NCPL, bool OUT_F32, bool XS>
+// Prepared activations, per 16-element chunk c: the 16 bytes at xb + 16c and
+// the constant zw*sum(x) - 16*zx*zw at xb + 16*chunks + 4c.
+template <int NCPL, bool OUT_F32, bool ZX>
 struct I8Op {
   using Params = I8OpParams;
+  static constexpr int kRawWords = 4;
   struct Lane {
-    uint32_t xr[XS ? 1 : NCPL][4];
-    int kl;  // sum over this lane's chunks of zw*sum(x) - 16*zx*zw
+    int kl;  // sum of the chunk constants over this lane's chunks
   };
 
-  __device__ __forceinline__ static void init(const Params &p, Lane &L, int lane, uint8_t *xs, int ctid) {
-    if (XS) {
-      for (int c = ctid; c < p.chunks; c += kConsumerWarps * 32) {
-        uint32_t X[4];
-        load_bytes(p.x + 16 * c, p.x_al16 != 0, X, 4);
-        reinterpret_cast<uint4 *>(xs)[c] = make_uint4(X[0], X[1], X[2], X[3]);
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-    }
+  static int xbuf_bytes(int chunks) { return ((chunks * 20 + 127) / 128) * 128; }
+
+  __device__ __forceinline__ static void load_raw(const int8_t *x, int c, bool al16, uint32_t (&raw)[4]) {
+    load_words<4>(x + 16 * c, al16, raw);
+  }
+
+  __device__ __forceinline__ static void store_prep(const Params &p, const uint32_t (&X)[4], int c, uint8_t *xb) {
+    int sumx = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) sumx = dp4a_ss(X[q], 0x01010101u, sumx);
+    reinterpret_cast<uint4 *>(xb)[c] = make_uint4(X[0], X[1], X[2], X[3]);
+    reinterpret_cast<uint32_t *>(xb + 16 * p.chunks)[c] =
+        (uint32_t)p.zw * (uint32_t)sumx - 16u * (uint32_t)p.zx * (uint32_t)p.zw;
+  }
+
+  __device__ __forceinline__ static void lane_init(const Params &p, Lane &L, const uint8_t *xb, int lane) {
     uint32_t kl = 0;
 #pragma unroll
     for (int j = 0; j < NCPL; ++j) {
       const int c = lane + 32 * j;
-      uint32_t X[4] = {0, 0, 0, 0};
-      if (c < p.chunks) {
-        if (XS) {
-          const uint4 v = lds128(xs + 16 * c);
-          X[0] = v.x; X[1] = v.y; X[2] = v.z; X[3] = v.w;
-        } else {
-          load_bytes(p.x + 16 * c, p.x_al16 != 0, X, 4);
-        }
-        int sumx = 0;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) sumx = dp4a_ss(X[q], 0x01010101u, sumx);
-        kl += (uint32_t)p.zw * (uint32_t)sumx - 16u * (uint32_t)p.zx * (uint32_t)p.zw;
-      }
-      if (!XS) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) L.xr[XS ? 0 : j][q] = X[q];
-      }
+      if (c < p.chunks) kl += lds_u32(xb + 16 * p.chunks + 4 * c);
     }
     L.kl = (int)kl;
   }
 
-  __device__ __forceinline__ static bool rows2(const Params &p, const Lane &L, const uint8_t *xs,
-                                               const uint8_t *wa, const uint8_t *, const uint8_t *wb,
-                                               const uint8_t *, int64_t ga, bool has_b, int lane) {
+  __device__ __forceinline__ static uint32_t rows2(const Params &p, const Lane &L, const uint8_t *xb,
+                                                   const uint8_t *wa, const uint8_t *, const uint8_t *wb,
+                                                   const uint8_t *, const GemvItem &it, int64_t ga, bool has_b,
+                                                   int lane) {
+    const float *ws = reinterpret_cast<const float *>(it.s);
     float wsa = 0.0f, wsb = 0.0f;
     if (OUT_F32) {  // issue the per-channel scale loads early
-      if (lane == 0) wsa = __ldg(p.ws + ga);
-      if (lane == 1 && has_b) wsb = __ldg(p.ws + ga + 1);
+      if (lane == 0) wsa = __ldg(ws + ga);
+      if (lane == 16 && has_b) wsb = __ldg(ws + ga + 1);
     }
     int acc_a = 0, acc_b = 0, sw_a = 0, sw_b = 0;
 #pragma unroll
     for (int j = 0; j < NCPL; ++j) {
       const int c = lane + 32 * j;
       if (c < p.chunks) {
-        uint32_t xr[4];
-        if (XS) {
-          const uint4 v = lds128(xs + 16 * c);
-          xr[0] = v.x; xr[1] = v.y; xr[2] = v.z; xr[3] = v.w;
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) xr[q] = L.xr[XS ? 0 : j][q];
-        }
+        const uint4 xr = lds128(xb + 16 * c);
         const uint4 va = lds128(wa + 16 * c);
         const uint4 vb = lds128(wb + 16 * c);
-        acc_a = dp4a_ss(va.x, xr[0], acc_a);
-        acc_b = dp4a_ss(vb.x, xr[0], acc_b);
-        acc_a = dp4a_ss(va.y, xr[1], acc_a);
-        acc_b = dp4a_ss(vb.y, xr[1], acc_b);
-        acc_a = dp4a_ss(va.z, xr[2], acc_a);
-        acc_b = dp4a_ss(vb.z, xr[2], acc_b);
-        acc_a = dp4a_ss(va.w, xr[3], acc_a);
-        acc_b = dp4a_ss(vb.w, xr[3], acc_b);
-        if (p.zx != 0) {
+        acc_a = dp4a_ss(va.x, xr.x, acc_a);
+        acc_b = dp4a_ss(vb.x, xr.x, acc_b);
+        acc_a = dp4a_ss(va.y, xr.y, acc_a);
+        acc_b = dp4a_ss(vb.y, xr.y, acc_b);
+        acc_a = dp4a_ss(va.z, xr.z, acc_a);
+        acc_b = dp4a_ss(vb.z, xr.z, acc_b);
+        acc_a = dp4a_ss(va.w, xr.w, acc_a);
+        acc_b = dp4a_ss(vb.w, xr.w, acc_b);
+        if (ZX) {
           sw_a = dp4a_ss(va.x, 0x01010101u, sw_a);
           sw_a = dp4a_ss(va.y, 0x01010101u, sw_a);
           sw_a = dp4a_ss(va.z, 0x01010101u, sw_a);
@@ -362,132 +355,187 @@ struct I8Op {
         }
       }
     }
-    uint32_t ta = (uint32_t)acc_a - (uint32_t)p.zx * (uint32_t)sw_a - (uint32_t)L.kl;
-    uint32_t tb = (uint32_t)acc_b - (uint32_t)p.zx * (uint32_t)sw_b - (uint32_t)L.kl;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      ta += __shfl_xor_sync(0xffffffffu, ta, o);
-      tb += __shfl_xor_sync(0xffffffffu, tb, o);
-    }
+    const uint32_t ta = (uint32_t)acc_a - (uint32_t)p.zx * (uint32_t)sw_a - (uint32_t)L.kl;
+    const uint32_t tb = (uint32_t)acc_b - (uint32_t)p.zx * (uint32_t)sw_b - (uint32_t)L.kl;
+    const uint32_t t = warp_sum_pair(ta, tb, lane);
     if (OUT_F32) {
-      if (lane == 0) reinterpret_cast<float *>(p.y)[ga] = __fmul_rn(__fmul_rn((float)(int)ta, wsa), p.sa);
-      if (lane == 1 && has_b)
-        reinterpret_cast<float *>(p.y)[ga + 1] = __fmul_rn(__fmul_rn((float)(int)tb, wsb), p.sa);
+      float *y = reinterpret_cast<float *>(it.y);
+      if (lane == 0) y[ga] = __fmul_rn(__fmul_rn((float)(int)t, wsa), p.sa);
+      if (lane == 16 && has_b) y[ga + 1] = __fmul_rn(__fmul_rn((float)(int)t, wsb), p.sa);
     } else {
-      if (lane == 0) reinterpret_cast<int32_t *>(p.y)[ga] = (int32_t)ta;
-      if (lane == 1 && has_b) reinterpret_cast<int32_t *>(p.y)[ga + 1] = (int32_t)tb;
+      int32_t *y = reinterpret_cast<int32_t *>(it.y);
+      if (lane == 0) y[ga] = (int32_t)t;
+      if (lane == 16 && has_b) y[ga + 1] = (int32_t)t;
     }
-    return false;
+    return 0;
   }
+
+  __device__ __forceinline__ static bool bad(uint32_t) { return false; }
 };
 
 // ------------------------------------------------------ streaming skeleton --
-template <class Op>
-__global__ void __launch_bounds__(kStreamThreads, 2)
-    gemv_stream_kernel(const StreamGeom g, const typename Op::Params op) {
+template <int CW>
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+}
+
+template <class Op, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
+    gemv_stream_kernel(const StreamGeom g, const typename Op::Params op, const GemvItems items) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + g.nst;
-  uint8_t *xs = smem + kBarBytes;
-  uint8_t *stages = xs + g.x_bytes;
+  uint8_t *xbufs = smem + kBarBytes;
+  uint8_t *stages = xbufs + 2 * g.xbuf_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t r0 = (int64_t)blockIdx.x * g.rows / g.n_cta;
   const int64_t r1 = (int64_t)(blockIdx.x + 1) * g.rows / g.n_cta;
   const int rows_cta = (int)(r1 - r0);
-  const int nstages = (rows_cta + g.rps - 1) / g.rps;
+  const int nstages = (rows_cta + g.rps - 1) / g.rps;  // per matrix
+  const int total = nstages * g.count;
 
   if (threadIdx.x == 0) {
     for (int b = 0; b < g.nst; ++b) {
       mbar_init(&full[b], 1);
-      mbar_init(&empty[b], kConsumerWarps);
+      mbar_init(&empty[b], CW);
     }
     fence_mbarrier_init();
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
+  if (warp == CW) {
     // ---------------- producer: one thread issues every bulk copy ----------
     // Weights and scales do not depend on the previous kernel: no wait here.
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      int issued = 0;
-      for (int st = 0; st < nstages; ++st) {
-        const int b = st % g.nst;
-        if (st == g.nst) pdl_launch_dependents();
-        if (st >= g.nst && !mbar_wait(&empty[b], (uint32_t)((st / g.nst) - 1) & 1u)) {
-          set_status(g.status, kStatusTimeout);
-          break;
-        }
-        const int lo = st * g.rps;
-        const int n = min(g.rps, rows_cta - lo);
-        const uint32_t wbytes = (uint32_t)n * (uint32_t)g.row_bytes;
-        const uint32_t sbytes = (uint32_t)n * (uint32_t)g.srow_bytes;
-        uint8_t *dst = stages + (size_t)b * g.stage_bytes;
-        mbar_arrive_expect_tx(&full[b], wbytes + sbytes);
-        const uint8_t *wsrc = g.w + (r0 + lo) * g.wstride;
-        if (g.w_contig) {
-          bulk_g2s_hint(dst, wsrc, wbytes, &full[b], pol);
-        } else {
-          for (int r = 0; r < n; ++r)
-            bulk_g2s_hint(dst + (size_t)r * g.row_bytes, wsrc + (int64_t)r * g.wstride, g.row_bytes,
-                          &full[b], pol);
-        }
-        if (g.srow_bytes) {
-          uint8_t *sdst = dst + (size_t)g.rps * g.row_bytes;
-          const uint8_t *ssrc = g.s + (r0 + lo) * g.sstride;
-          if (g.s_contig) {
-            bulk_g2s(sdst, ssrc, sbytes, &full[b]);
+      int gs = 0;
+      bool stop = false;
+      for (int m = 0; m < g.count && !stop; ++m) {
+        const GemvItem &it = items.it[m];
+        for (int st = 0; st < nstages; ++st, ++gs) {
+          const int b = gs % g.nst;
+          if (gs == g.nst) pdl_launch_dependents();
+          if (gs >= g.nst && !mbar_wait(&empty[b], (uint32_t)((gs / g.nst) - 1) & 1u)) {
+            set_status(g.status, kStatusTimeout);
+            stop = true;
+            break;
+          }
+          const int lo = st * g.rps;
+          const int n = min(g.rps, rows_cta - lo);
+          const uint32_t wbytes = (uint32_t)n * (uint32_t)g.row_bytes;
+          const uint32_t sbytes = (uint32_t)n * (uint32_t)g.srow_bytes;
+          uint8_t *dst = stages + (size_t)b * g.stage_bytes;
+          mbar_arrive_expect_tx(&full[b], wbytes + sbytes);
+          const uint8_t *wsrc = it.w + (r0 + lo) * g.wstride;
+          if (g.w_contig) {
+            bulk_g2s_hint(dst, wsrc, wbytes, &full[b], pol);
           } else {
             for (int r = 0; r < n; ++r)
-              bulk_g2s(sdst + (size_t)r * g.srow_bytes, ssrc + (int64_t)r * g.sstride, g.srow_bytes,
-                       &full[b]);
+              bulk_g2s_hint(dst + (size_t)r * g.row_bytes, wsrc + (int64_t)r * g.wstride, g.row_bytes,
+                            &full[b], pol);
+          }
+          if (g.srow_bytes) {
+            uint8_t *sdst = dst + (size_t)g.rps * g.row_bytes;
+            const uint8_t *ssrc = it.s + (r0 + lo) * g.sstride;
+            if (g.s_contig) {
+              bulk_g2s(sdst, ssrc, sbytes, &full[b]);
+            } else {
+              for (int r = 0; r < n; ++r)
+                bulk_g2s(sdst + (size_t)r * g.srow_bytes, ssrc + (int64_t)r * g.sstride, g.srow_bytes,
+                         &full[b]);
+            }
           }
         }
-        ++issued;
       }
-      if (nstages <= g.nst) pdl_launch_dependents();
+      if (total <= g.nst) pdl_launch_dependents();
       // Before the CTA may exit, every copy it issued must have landed.
-      for (int st = max(0, issued - g.nst); st < issued; ++st) {
-        if (!mbar_wait(&full[st % g.nst], (uint32_t)(st / g.nst) & 1u)) set_status(g.status, kStatusTimeout);
+      for (int s2 = max(0, gs - g.nst); s2 < gs; ++s2) {
+        if (!mbar_wait(&full[s2 % g.nst], (uint32_t)(s2 / g.nst) & 1u)) set_status(g.status, kStatusTimeout);
       }
     }
     return;
   }
 
   // ------------------------------------------------------------ consumers --
-  // The activation vector (and the output) belong to the previous kernel on
-  // the stream until it has completed.
+  // Activations (and outputs) belong to the previous kernel on the stream
+  // until it has completed.
   pdl_wait();
-  typename Op::Lane L;
-  Op::init(op, L, lane, xs, threadIdx.x);
-  bool bad = false;
-  for (int st = 0; st < nstages; ++st) {
-    const int b = st % g.nst;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[b], (uint32_t)(st / g.nst) & 1u));
-    if (!ok) {
-      if (lane == 0) set_status(g.status, kStatusTimeout);
-      break;
-    }
-    const int lo = st * g.rps;
-    const int hi = min(lo + g.rps, rows_cta);
-    const uint8_t *base = stages + (size_t)b * g.stage_bytes;
-    const uint8_t *sbase = base + (size_t)g.rps * g.row_bytes;
-    // row pairs (lo + 2q, lo + 2q + 1); pair q goes to warp (lo/2 + q) % warps
-    const int pair0 = lo / 2;
-    int q = ((warp - pair0 % kConsumerWarps) + kConsumerWarps) % kConsumerWarps;
-    for (; lo + 2 * q < hi; q += kConsumerWarps) {
-      const int i = lo + 2 * q;
-      const int li = i - lo;
-      bad |= Op::rows2(op, L, xs, base + (size_t)li * g.row_bytes, sbase + (size_t)li * g.srow_bytes,
-                       base + (size_t)(li + 1) * g.row_bytes, sbase + (size_t)(li + 1) * g.srow_bytes, r0 + i,
-                       i + 1 < hi, lane);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[b]);
+  const int ctid = threadIdx.x;
+  constexpr int NT = CW * 32;
+  constexpr int RW = Op::kRawWords;
+  for (int c = ctid; c < op.chunks; c += NT) {
+    uint32_t raw[RW];
+    Op::load_raw(items.it[0].x, c, g.x_al16 != 0, raw);
+    Op::store_prep(op, raw, c, xbufs);
   }
-  if (__any_sync(0xffffffffu, bad) && lane == 0) set_status(g.status, kStatusBadScale);
+  consumers_sync<CW>();
+
+  const bool prefetch = op.chunks <= 2 * NT;  // next matrix's raw x fits in registers
+  uint32_t mx = 0;
+  int gs = 0;
+  int pair_base = 0;
+  bool stop = false;
+  for (int m = 0; m < g.count && !stop; ++m) {
+    const GemvItem &it = items.it[m];
+    const uint8_t *xb = xbufs + (size_t)(m & 1) * g.xbuf_bytes;
+    uint32_t pre[2][RW];
+    const bool more = m + 1 < g.count;
+    if (more && prefetch) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = ctid + k * NT;
+        if (c < op.chunks) Op::load_raw(items.it[m + 1].x, c, g.x_al16 != 0, pre[k]);
+      }
+    }
+    typename Op::Lane L;
+    Op::lane_init(op, L, xb, lane);
+    for (int st = 0; st < nstages; ++st, ++gs) {
+      const int b = gs % g.nst;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[b], (uint32_t)(gs / g.nst) & 1u));
+      if (!ok) {
+        if (lane == 0) set_status(g.status, kStatusTimeout);
+        stop = true;
+        break;
+      }
+      const int lo = st * g.rps;
+      const int hi = min(lo + g.rps, rows_cta);
+      const uint8_t *base = stages + (size_t)b * g.stage_bytes;
+      const uint8_t *sbase = base + (size_t)g.rps * g.row_bytes;
+      // row pairs (lo + 2q, lo + 2q + 1); the pair's running index across the
+      // launch picks the warp, so stages alternate between warp groups
+      const int pair0 = pair_base + lo / 2;
+      int q = ((warp - pair0 % CW) + CW) % CW;
+      for (; lo + 2 * q < hi; q += CW) {
+        const int li = 2 * q;
+        mx = max(mx, Op::rows2(op, L, xb, base + (size_t)li * g.row_bytes, sbase + (size_t)li * g.srow_bytes,
+                               base + (size_t)(li + 1) * g.row_bytes, sbase + (size_t)(li + 1) * g.srow_bytes,
+                               it, r0 + lo + li, lo + li + 1 < hi, lane));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[b]);
+    }
+    pair_base += (rows_cta + 1) / 2;
+    if (more && !stop) {
+      uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
+      if (prefetch) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int c = ctid + k * NT;
+          if (c < op.chunks) Op::store_prep(op, pre[k], c, xn);
+        }
+      } else {
+        for (int c = ctid; c < op.chunks; c += NT) {
+          uint32_t raw[RW];
+          Op::load_raw(items.it[m + 1].x, c, g.x_al16 != 0, raw);
+          Op::store_prep(op, raw, c, xn);
+        }
+      }
+      consumers_sync<CW>();
+    }
+  }
+  if (__any_sync(0xffffffffu, Op::bad(mx)) && lane == 0) set_status(g.status, kStatusBadScale);
 }
 
 // ------------------------------------------------------- generic kernels --
@@ -565,24 +613,28 @@ int ilog2_exact(int64_t v) {
   return s;
 }
 
-// Fill the ring geometry; false if the rows are too long to stage.
-bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int x_bytes, int sm_count) {
-  static const int smem_cta = std::min(kSmemPerCta, env_int("KS_B200_SMEM_PER_CTA", kSmemPerCta));
-  static const int min_stages = std::max(2, env_int("KS_B200_MIN_STAGES", 3));
+// Fill the ring geometry for one configuration (single or batch); false if
+// the rows are too long to stage.
+bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int xbuf_bytes, int sm_count,
+                 bool batch, int cw) {
+  static const int min_single = std::max(2, env_int("KS_B200_MIN_STAGES", 2));
+  static const int rps_cap_batch = std::max(2, env_int("KS_B200_BATCH_ROWS_PER_STAGE", 24));
+  const int smem_cta = batch ? kSmemBatch : kSmemSingle;
+  const int min_stages = batch ? 4 : min_single;
   const int row_total = row_bytes + srow_bytes;
-  const int budget = smem_cta - kBarBytes - x_bytes;
+  const int budget = smem_cta - kBarBytes - 2 * xbuf_bytes;
+  if (budget <= 0) return false;
   const int64_t n_cta = std::min<int64_t>(rows, sm_count);
   const int64_t rows_cta_max = (rows + n_cta - 1) / n_cta;
   int rps = (budget / min_stages) / row_total;
-  rps = std::min(rps, 2 * kConsumerWarps);
+  rps = std::min(rps, batch ? rps_cap_batch : 2 * cw);
   rps = (int)std::min<int64_t>(rps, (rows_cta_max + 1) & ~int64_t(1));
   rps &= ~1;
   if (rps < 2) rps = 2;
   const int stage_bytes = ((rps * row_total + 127) / 128) * 128;
   int nst = budget / stage_bytes;
-  const int64_t need = (rows_cta_max + rps - 1) / rps;
-  nst = (int)std::min<int64_t>(std::min(nst, kMaxStages), need);
-  if (nst < 1 || (nst < 2 && need > 1)) return false;
+  nst = std::min(nst, kMaxStages);
+  if (nst < 2) return false;
   g.rows = rows;
   g.n_cta = (int32_t)n_cta;
   g.rps = rps;
@@ -590,12 +642,12 @@ bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int
   g.row_bytes = row_bytes;
   g.srow_bytes = srow_bytes;
   g.stage_bytes = stage_bytes;
-  g.x_bytes = x_bytes;
+  g.xbuf_bytes = xbuf_bytes;
   return true;
 }
 
 size_t stream_smem_bytes(const StreamGeom &g) {
-  return (size_t)kBarBytes + (size_t)g.x_bytes + (size_t)g.nst * g.stage_bytes;
+  return (size_t)kBarBytes + 2 * (size_t)g.xbuf_bytes + (size_t)g.nst * g.stage_bytes;
 }
 
 bool pdl_enabled(cudaStream_t stream) {
@@ -603,20 +655,21 @@ bool pdl_enabled(cudaStream_t stream) {
   return on && stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread;
 }
 
-template <class Op>
-cudaError_t launch_stream(const StreamGeom &g, const typename Op::Params &op, cudaStream_t stream, int dev) {
-  const size_t smem = stream_smem_bytes(g);
+template <class Op, int CW>
+cudaError_t launch_stream(const StreamGeom &g, const typename Op::Params &op, const GemvItems &items,
+                          cudaStream_t stream, int dev) {
   static std::once_flag attr_once[64];
   static cudaError_t attr_err[64];
   std::call_once(attr_once[dev & 63], [&] {
-    attr_err[dev & 63] = cudaFuncSetAttribute(gemv_stream_kernel<Op>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemPerCta);
+    const int want = std::min(device_props(dev).smem_optin, CW <= 8 ? kSmemSingle : kSmemBatch);
+    attr_err[dev & 63] =
+        cudaFuncSetAttribute(gemv_stream_kernel<Op, CW>, cudaFuncAttributeMaxDynamicSharedMemorySize, want);
   });
   if (attr_err[dev & 63] != cudaSuccess) return attr_err[dev & 63];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)g.n_cta);
-  cfg.blockDim = dim3(kStreamThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.blockDim = dim3((CW + 1) * 32);
+  cfg.dynamicSmemBytes = stream_smem_bytes(g);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   if (pdl_enabled(stream)) {
@@ -625,9 +678,14 @@ cudaError_t launch_stream(const StreamGeom &g, const typename Op::Params &op, cu
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<Op>, g, op);
+  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<Op, CW>, g, op, items);
 }
 
+int ncpl_of(int chunks) {
+  return chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;
+}
+
+// ---- W4A8 ---------------------------------------------------------------
 struct W4A8Plan {
   bool fast = false;
   StreamGeom g{};
@@ -635,56 +693,63 @@ struct W4A8Plan {
   int ncpl = 0;
 };
 
-constexpr int kMaxStreamChunks = 512;  // W4A8 rows up to 16384 columns, INT8 up to 8192
-
-W4A8Plan plan_w4a8(const W4A8Launch &a, int device) {
-  W4A8Plan P;
+bool w4a8_shape_ok(const W4A8Launch &a) {
   const int ssize = a.stype == kScaleF16 ? 2 : 4;
   const int64_t groups = (a.cols + a.group - 1) / a.group;
-  const int gshift = ilog2_exact(a.group / 32);
-  const bool shape_ok = a.cols % 32 == 0 && a.group % 32 == 0 && gshift >= 0 &&
-                        a.cols / 32 <= kMaxStreamChunks && a.wstride % 16 == 0 && aligned16(a.w) &&
-                        (groups * ssize) % 16 == 0 && (a.sstride * ssize) % 16 == 0 && aligned16(a.s) &&
-                        a.rows < (int64_t(1) << 31);
-  if (!shape_ok) return P;
-  const DeviceProps &dp = device_props(device);
+  return a.cols % 32 == 0 && a.group % 32 == 0 && ilog2_exact(a.group / 32) >= 0 &&
+         a.cols / 32 <= kMaxStreamChunks && a.wstride % 16 == 0 && (groups * ssize) % 16 == 0 &&
+         (a.sstride * ssize) % 16 == 0 && a.rows < (int64_t(1) << 31);
+}
+
+W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch) {
+  W4A8Plan P;
+  if (!w4a8_shape_ok(a)) return P;
+  const int ssize = a.stype == kScaleF16 ? 2 : 4;
+  const int64_t groups = (a.cols + a.group - 1) / a.group;
   const int chunks = (int)(a.cols / 32);
-  P.ncpl = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;
-  const bool xs = P.ncpl > 4;
-  const int x_bytes = xs ? ((chunks * 36 + 127) / 128) * 128 : 0;
+  const int xbuf = ((chunks * 36 + 127) / 128) * 128;
   StreamGeom g{};
-  if (!plan_stream(g, a.rows, (int)(a.cols / 2), (int)(groups * ssize), x_bytes, dp.sm_count)) return P;
-  g.w = a.w;
+  if (!plan_stream(g, a.rows, (int)(a.cols / 2), (int)(groups * ssize), xbuf, device_props(device).sm_count,
+                   batch, batch ? 16 : 8))
+    return P;
   g.wstride = a.wstride;
-  g.s = reinterpret_cast<const uint8_t *>(a.s);
   g.sstride = a.sstride * ssize;
   g.w_contig = a.wstride == a.cols / 2;
   g.s_contig = g.sstride == g.srow_bytes;
   g.status = a.status;
   P.g = g;
-  P.op.x = a.x;
-  P.op.y = a.y;
   P.op.chunks = chunks;
-  P.op.gshift = gshift;
+  P.op.gshift = ilog2_exact(a.group / 32);
   P.op.sx = a.sx;
   P.op.zx = a.zx;
   P.op.zw = a.zw;
-  P.op.x_al16 = aligned16(a.x);
+  P.ncpl = ncpl_of(chunks);
   P.fast = true;
   return P;
 }
 
-template <typename ST>
-cudaError_t launch_w4a8_fast(const W4A8Plan &P, cudaStream_t stream, int dev) {
+template <typename ST, bool ZX, int CW>
+cudaError_t launch_w4a8_ncpl(const W4A8Plan &P, const GemvItems &items, cudaStream_t stream, int dev) {
   switch (P.ncpl) {
-    case 1: return launch_stream<W4A8Op<ST, 1, false>>(P.g, P.op, stream, dev);
-    case 2: return launch_stream<W4A8Op<ST, 2, false>>(P.g, P.op, stream, dev);
-    case 4: return launch_stream<W4A8Op<ST, 4, false>>(P.g, P.op, stream, dev);
-    case 8: return launch_stream<W4A8Op<ST, 8, true>>(P.g, P.op, stream, dev);
-    default: return launch_stream<W4A8Op<ST, 16, true>>(P.g, P.op, stream, dev);
+    case 1: return launch_stream<W4A8Op<ST, 1, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 2: return launch_stream<W4A8Op<ST, 2, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 4: return launch_stream<W4A8Op<ST, 4, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 8: return launch_stream<W4A8Op<ST, 8, ZX>, CW>(P.g, P.op, items, stream, dev);
+    default: return launch_stream<W4A8Op<ST, 16, ZX>, CW>(P.g, P.op, items, stream, dev);
   }
 }
 
+template <int CW>
+cudaError_t launch_w4a8_cw(const W4A8Plan &P, int stype, const GemvItems &items, cudaStream_t stream, int dev) {
+  const bool zx = P.op.zx != 0;
+  if (stype == kScaleF16)
+    return zx ? launch_w4a8_ncpl<__half, true, CW>(P, items, stream, dev)
+              : launch_w4a8_ncpl<__half, false, CW>(P, items, stream, dev);
+  return zx ? launch_w4a8_ncpl<float, true, CW>(P, items, stream, dev)
+            : launch_w4a8_ncpl<float, false, CW>(P, items, stream, dev);
+}
+
+// ---- INT8 ---------------------------------------------------------------
 struct I8Plan {
   bool fast = false;
   StreamGeom g{};
@@ -692,52 +757,98 @@ struct I8Plan {
   int ncpl = 0;
 };
 
-I8Plan plan_i8(const I8Launch &a, int device) {
+bool i8_shape_ok(const I8Launch &a) {
+  return a.cols % 16 == 0 && a.cols / 16 <= kMaxStreamChunks && a.wstride % 16 == 0 &&
+         a.rows < (int64_t(1) << 31);
+}
+
+I8Plan plan_i8(const I8Launch &a, int device, bool batch) {
   I8Plan P;
-  const bool shape_ok = a.cols % 16 == 0 && a.cols / 16 <= kMaxStreamChunks && a.wstride % 16 == 0 &&
-                        aligned16(a.w) && a.rows < (int64_t(1) << 31);
-  if (!shape_ok) return P;
-  const DeviceProps &dp = device_props(device);
+  if (!i8_shape_ok(a)) return P;
   const int chunks = (int)(a.cols / 16);
-  P.ncpl = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;
-  const bool xs = P.ncpl > 8;
-  const int x_bytes = xs ? ((chunks * 16 + 127) / 128) * 128 : 0;
+  const int xbuf = ((chunks * 20 + 127) / 128) * 128;
   StreamGeom g{};
-  if (!plan_stream(g, a.rows, (int)a.cols, 0, x_bytes, dp.sm_count)) return P;
-  g.w = reinterpret_cast<const uint8_t *>(a.w);
+  if (!plan_stream(g, a.rows, (int)a.cols, 0, xbuf, device_props(device).sm_count, batch, batch ? 16 : 8))
+    return P;
   g.wstride = a.wstride;
-  g.s = nullptr;
   g.sstride = 0;
   g.w_contig = a.wstride == a.cols;
   g.s_contig = 1;
   g.status = a.status;
   P.g = g;
-  P.op.x = a.x;
-  P.op.y = a.y;
-  P.op.ws = a.ws;
   P.op.sa = a.sa;
   P.op.chunks = chunks;
   P.op.zx = a.zx;
   P.op.zw = a.zw;
-  P.op.x_al16 = aligned16(a.x);
+  P.ncpl = ncpl_of(chunks);
   P.fast = true;
   return P;
 }
 
-template <bool F32>
-cudaError_t launch_i8_fast(const I8Plan &P, cudaStream_t stream, int dev) {
+template <bool F32, bool ZX, int CW>
+cudaError_t launch_i8_ncpl(const I8Plan &P, const GemvItems &items, cudaStream_t stream, int dev) {
   switch (P.ncpl) {
-    case 1: return launch_stream<I8Op<1, F32, false>>(P.g, P.op, stream, dev);
-    case 2: return launch_stream<I8Op<2, F32, false>>(P.g, P.op, stream, dev);
-    case 4: return launch_stream<I8Op<4, F32, false>>(P.g, P.op, stream, dev);
-    case 8: return launch_stream<I8Op<8, F32, false>>(P.g, P.op, stream, dev);
-    default: return launch_stream<I8Op<16, F32, true>>(P.g, P.op, stream, dev);
+    case 1: return launch_stream<I8Op<1, F32, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 2: return launch_stream<I8Op<2, F32, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 4: return launch_stream<I8Op<4, F32, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 8: return launch_stream<I8Op<8, F32, ZX>, CW>(P.g, P.op, items, stream, dev);
+    default: return launch_stream<I8Op<16, F32, ZX>, CW>(P.g, P.op, items, stream, dev);
   }
+}
+
+template <int CW>
+cudaError_t launch_i8_cw(const I8Plan &P, bool f32, const GemvItems &items, cudaStream_t stream, int dev) {
+  const bool zx = P.op.zx != 0;
+  if (f32)
+    return zx ? launch_i8_ncpl<true, true, CW>(P, items, stream, dev)
+              : launch_i8_ncpl<true, false, CW>(P, items, stream, dev);
+  return zx ? launch_i8_ncpl<false, true, CW>(P, items, stream, dev)
+            : launch_i8_ncpl<false, false, CW>(P, items, stream, dev);
 }
 
 int generic_grid(int64_t rows, int sm_count) {
   const int64_t blocks = (rows + 7) / 8;
   return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sm_count * 8));
+}
+
+cudaError_t launch_w4a8_generic(const W4A8Launch &a, cudaStream_t stream, int device) {
+  const int grid = generic_grid(a.rows, device_props(device).sm_count);
+  if (a.stype == kScaleF16) {
+    w4a8_generic_kernel<__half><<<grid, 256, 0, stream>>>(
+        a.x, a.w, a.wstride, reinterpret_cast<const __half *>(a.s), a.sstride, a.y, a.rows, a.cols, a.group,
+        a.sx, a.zx, a.zw, a.status);
+  } else {
+    w4a8_generic_kernel<float><<<grid, 256, 0, stream>>>(
+        a.x, a.w, a.wstride, reinterpret_cast<const float *>(a.s), a.sstride, a.y, a.rows, a.cols, a.group,
+        a.sx, a.zx, a.zw, a.status);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_i8_generic(const I8Launch &a, cudaStream_t stream, int device) {
+  const int grid = generic_grid(a.rows, device_props(device).sm_count);
+  if (a.out_f32) {
+    i8_generic_kernel<true><<<grid, 256, 0, stream>>>(a.x, a.w, a.wstride, a.y, a.rows, a.cols, a.zx, a.zw,
+                                                      a.ws, a.sa);
+  } else {
+    i8_generic_kernel<false><<<grid, 256, 0, stream>>>(a.x, a.w, a.wstride, a.y, a.rows, a.cols, a.zx, a.zw,
+                                                       a.ws, a.sa);
+  }
+  return cudaGetLastError();
+}
+
+bool batch_aligned(const GemvBatch &b, bool need_s) {
+  for (int i = 0; i < b.count; ++i) {
+    if (!aligned16(b.w[i])) return false;
+    if (need_s && !aligned16(b.s[i])) return false;
+  }
+  return true;
+}
+
+bool batch_x_aligned(const GemvBatch &b, int from, int n) {
+  for (int i = from; i < from + n; ++i)
+    if (!aligned16(b.x[i])) return false;
+  return true;
 }
 
 }  // namespace
@@ -758,48 +869,99 @@ const DeviceProps &device_props(int device) {
 int w4a8_path(const W4A8Launch &a) {
   int dev = 0;
   cudaGetDevice(&dev);
-  return plan_w4a8(a, dev).fast ? 1 : 0;
+  return (aligned16(a.w) && aligned16(a.s) && plan_w4a8(a, dev, false).fast) ? 1 : 0;
 }
 
 int i8_path(const I8Launch &a) {
   int dev = 0;
   cudaGetDevice(&dev);
-  return plan_i8(a, dev).fast ? 1 : 0;
+  return (aligned16(a.w) && plan_i8(a, dev, false).fast) ? 1 : 0;
 }
 
 cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device) {
-  const W4A8Plan P = plan_w4a8(a, device);
-  if (P.fast) {
-    return a.stype == kScaleF16 ? launch_w4a8_fast<__half>(P, stream, device)
-                                : launch_w4a8_fast<float>(P, stream, device);
+  W4A8Plan P;
+  if (aligned16(a.w) && aligned16(a.s)) P = plan_w4a8(a, device, false);
+  if (!P.fast) return launch_w4a8_generic(a, stream, device);
+  GemvItems items;
+  items.it[0] = GemvItem{a.x, a.w, reinterpret_cast<const uint8_t *>(a.s), a.y};
+  P.g.count = 1;
+  P.g.x_al16 = aligned16(a.x);
+  return launch_w4a8_cw<8>(P, a.stype, items, stream, device);
+}
+
+cudaError_t launch_w4a8_batch(const W4A8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device) {
+  if (b.count <= 0) return cudaSuccess;
+  W4A8Plan P;
+  if (batch_aligned(b, true)) P = plan_w4a8(shape, device, b.count > 1);
+  for (int i0 = 0; i0 < b.count; i0 += kMaxItems) {
+    const int n = std::min(kMaxItems, b.count - i0);
+    cudaError_t e;
+    if (!P.fast) {
+      for (int i = i0; i < i0 + n; ++i) {
+        W4A8Launch a = shape;
+        a.x = b.x[i];
+        a.w = static_cast<const uint8_t *>(b.w[i]);
+        a.s = b.s[i];
+        a.y = static_cast<float *>(b.y[i]);
+        if ((e = launch_w4a8_generic(a, stream, device)) != cudaSuccess) return e;
+      }
+      continue;
+    }
+    GemvItems items;
+    for (int i = 0; i < n; ++i)
+      items.it[i] = GemvItem{b.x[i0 + i], static_cast<const uint8_t *>(b.w[i0 + i]),
+                             static_cast<const uint8_t *>(b.s[i0 + i]), b.y[i0 + i]};
+    W4A8Plan Q = P;
+    Q.g.count = n;
+    Q.g.x_al16 = batch_x_aligned(b, i0, n);
+    e = b.count > 1 ? launch_w4a8_cw<16>(Q, shape.stype, items, stream, device)
+                    : launch_w4a8_cw<8>(Q, shape.stype, items, stream, device);
+    if (e != cudaSuccess) return e;
   }
-  const int grid = generic_grid(a.rows, device_props(device).sm_count);
-  if (a.stype == kScaleF16) {
-    w4a8_generic_kernel<__half><<<grid, 256, 0, stream>>>(
-        a.x, a.w, a.wstride, reinterpret_cast<const __half *>(a.s), a.sstride, a.y, a.rows, a.cols,
-        a.group, a.sx, a.zx, a.zw, a.status);
-  } else {
-    w4a8_generic_kernel<float><<<grid, 256, 0, stream>>>(
-        a.x, a.w, a.wstride, reinterpret_cast<const float *>(a.s), a.sstride, a.y, a.rows, a.cols,
-        a.group, a.sx, a.zx, a.zw, a.status);
-  }
-  return cudaGetLastError();
+  return cudaSuccess;
 }
 
 cudaError_t launch_i8(const I8Launch &a, cudaStream_t stream, int device) {
-  const I8Plan P = plan_i8(a, device);
-  if (P.fast) {
-    return a.out_f32 ? launch_i8_fast<true>(P, stream, device) : launch_i8_fast<false>(P, stream, device);
+  I8Plan P;
+  if (aligned16(a.w)) P = plan_i8(a, device, false);
+  if (!P.fast) return launch_i8_generic(a, stream, device);
+  GemvItems items;
+  items.it[0] = GemvItem{a.x, reinterpret_cast<const uint8_t *>(a.w), reinterpret_cast<const uint8_t *>(a.ws), a.y};
+  P.g.count = 1;
+  P.g.x_al16 = aligned16(a.x);
+  return launch_i8_cw<8>(P, a.out_f32 != 0, items, stream, device);
+}
+
+cudaError_t launch_i8_batch(const I8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device) {
+  if (b.count <= 0) return cudaSuccess;
+  I8Plan P;
+  if (batch_aligned(b, false)) P = plan_i8(shape, device, b.count > 1);
+  for (int i0 = 0; i0 < b.count; i0 += kMaxItems) {
+    const int n = std::min(kMaxItems, b.count - i0);
+    cudaError_t e;
+    if (!P.fast) {
+      for (int i = i0; i < i0 + n; ++i) {
+        I8Launch a = shape;
+        a.x = b.x[i];
+        a.w = static_cast<const int8_t *>(b.w[i]);
+        a.ws = static_cast<const float *>(b.s ? b.s[i] : nullptr);
+        a.y = b.y[i];
+        if ((e = launch_i8_generic(a, stream, device)) != cudaSuccess) return e;
+      }
+      continue;
+    }
+    GemvItems items;
+    for (int i = 0; i < n; ++i)
+      items.it[i] = GemvItem{b.x[i0 + i], static_cast<const uint8_t *>(b.w[i0 + i]),
+                             static_cast<const uint8_t *>(b.s ? b.s[i0 + i] : nullptr), b.y[i0 + i]};
+    I8Plan Q = P;
+    Q.g.count = n;
+    Q.g.x_al16 = batch_x_aligned(b, i0, n);
+    e = b.count > 1 ? launch_i8_cw<16>(Q, shape.out_f32 != 0, items, stream, device)
+                    : launch_i8_cw<8>(Q, shape.out_f32 != 0, items, stream, device);
+    if (e != cudaSuccess) return e;
   }
-  const int grid = generic_grid(a.rows, device_props(device).sm_count);
-  if (a.out_f32) {
-    i8_generic_kernel<true><<<grid, 256, 0, stream>>>(a.x, a.w, a.wstride, a.y, a.rows, a.cols,
-                                                      a.zx, a.zw, a.ws, a.sa);
-  } else {
-    i8_generic_kernel<false><<<grid, 256, 0, stream>>>(a.x, a.w, a.wstride, a.y, a.rows, a.cols,
-                                                       a.zx, a.zw, a.ws, a.sa);
-  }
-  return cudaGetLastError();
+  return cudaSuccess;
 }
 
 }  // namespace ksb

@@ -70,6 +70,21 @@ const DeviceProps &device_props(int device);
 
 cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device);
 cudaError_t launch_i8(const I8Launch &a, cudaStream_t stream, int device);
+
+// A batch of independent GEMVs of one shape: per-matrix activation, weight,
+// scale (W4A8 group scales or INT8 per-channel dequant scales) and output
+// pointers, host arrays of `count` entries.  Launched as one streaming pass
+// per SM; the shape fields of the W4A8Launch / I8Launch are used, their
+// pointer fields are not.
+struct GemvBatch {
+  int count;
+  const int8_t *const *x;
+  const void *const *w;
+  const void *const *s;
+  void *const *y;
+};
+cudaError_t launch_w4a8_batch(const W4A8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device);
+cudaError_t launch_i8_batch(const I8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device);
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
 
 // Which kernel family launch_w4a8 / launch_i8 picked for a shape (tests and

@@ -77,6 +77,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [_vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _i32, _i32, _vp],
     ),
+    "ks_b200_matvec_w4a8_batch_async": (
+        c_int,
+        [c_int, _vp, _vp, _vp, _vp, _sz, c_int, _sz, _sz, _sz, _sz, _f, _i32, _i32, _vp, _vp],
+    ),
+    "ks_b200_matvec_i8_batch_async": (c_int, [c_int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _i32, _i32, _f, _vp]),
     "ks_b200_gemm_i8_requant": (c_int, [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz]),
     "ks_b200_gemm_i8_requant_async": (
         c_int,
@@ -177,6 +182,35 @@ def gemm_i8_requant_async(a, sa, w, ws, out_scale, out, m, n, k, lda=None, ldw=N
         lib().ks_b200_gemm_i8_requant_async(
             addr(a), lda or k, addr(sa), addr(w), ldw or k, addr(ws), out_scale, addr(out), ldo or n, m, n, k,
             addr(acc_out), addr(status), stream_handle(stream),
+        )
+    )
+
+
+def _ptr_array(objs):
+    arr = (c_void_p * len(objs))(*[addr(o) for o in objs])
+    return arr
+
+
+def matvec_w4a8_batch_async(xs, ws, ss, ys, w_stride, s_stride, rows, cols, group, sx, zx=0, zw=0,
+                            scale_type=SCALE_F16, status=None, stream=None) -> None:
+    """Queue len(xs) independent W4A8 GEMVs of one shape as one launch."""
+    n = len(xs)
+    assert len(ws) == len(ss) == len(ys) == n
+    check(
+        lib().ks_b200_matvec_w4a8_batch_async(
+            n, _ptr_array(xs), _ptr_array(ws), _ptr_array(ss), _ptr_array(ys), w_stride, scale_type, s_stride,
+            rows, cols, group, sx, zx, zw, addr(status), stream_handle(stream),
+        )
+    )
+
+
+def matvec_i8_batch_async(xs, ws, ys, w_stride, rows, cols, zx=0, zw=0, w_scales=None, sa=1.0,
+                          stream=None) -> None:
+    n = len(xs)
+    check(
+        lib().ks_b200_matvec_i8_batch_async(
+            n, _ptr_array(xs), _ptr_array(ws), _ptr_array(w_scales) if w_scales is not None else None,
+            _ptr_array(ys), w_stride, rows, cols, zx, zw, sa, stream_handle(stream),
         )
     )
 
