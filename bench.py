@@ -60,10 +60,10 @@ CHUNKS = 4
 SEED = 20261201
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the W4A8 kernel
-# on this workload, from the ncu capture summarised in
-# profiles/w4a8_gemv_11008x4096_g32.md (None until captured).
-NCU_TRAFFIC_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of the batched W4A8 kernel on
+# this workload, per GEMV (one ncu launch = 16 GEMVs: 405,938,176 + 3,531,520
+# bytes), from the capture summarised in profiles/w4a8_gemv_11008x4096_g32.md.
+NCU_TRAFFIC_PER_GEMV = (405_938_176 + 3_531_520) // 16
 
 
 def gemv_bytes(rows=ROWS, cols=COLS, group=GROUP, scale_bytes=2) -> int:
@@ -403,7 +403,7 @@ def run_b200_arm(args):
             "config": workload_config(world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "traffic": NCU_TRAFFIC_PER_GEMV, "traffic_per": "GEMV (ncu capture)",
                          "kernel": "gemv_stream_kernel<W4A8Op<__half,4,false>,16> (batched, 16 GEMVs per launch)",
                          "bytes_per_gemv": gemv_bytes(), "us_per_gemv": per_launch_s * 1e6,
                          "gemvs_per_launch": MATS // CHUNKS},
