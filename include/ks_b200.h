@@ -76,6 +76,39 @@ int ks_b200_matvec_w4a8_f16(const int8_t *input, const uint8_t *packed_weights,
                             int32_t weight_zero_point);
 
 /*
+ * ks_b200_matvec_w4a8_f16 for callers that must not let a library allocate
+ * memory.  This entry point has no counterpart in the reference library.
+ *
+ * The other synchronous entry points allocate their scratch (staging copies
+ * of host buffers, status words) on first use.  Callers that reserve all
+ * device memory up front, hand device memory out through their own
+ * allocator, or run on threads where an allocation is not allowed use this
+ * one instead: it calls no cudaMalloc, cudaFree or other allocating routine.
+ * Its scratch is a fixed 540,928-byte array in device memory that every GPU
+ * which loads the library holds until the process exits.
+ *
+ * Same arguments, checks, results and return codes as
+ * ks_b200_matvec_w4a8_f16, with these limits:
+ *   - rows <= 131072 and cols <= 16384, else KS_ERR_INVALID_ARG;
+ *   - packed_weights and weight_scales_f16 must be device memory (they are
+ *     not staged), else KS_ERR_INVALID_ARG; input and output may be host
+ *     or device memory;
+ *   - the first call on a device looks up the scratch array's device address
+ *     for that device, so make it before any stream capture;
+ *   - every call uses the same scratch array: calls whose work overlaps on
+ *     the GPU (from several host threads) race and must be serialised.
+ */
+int ks_b200_matvec_w4a8_f16_noalloc(const int8_t *input,
+                                    const uint8_t *packed_weights,
+                                    size_t packed_stride_bytes,
+                                    const uint16_t *weight_scales_f16,
+                                    size_t scale_stride, float *output,
+                                    size_t rows, size_t cols,
+                                    size_t group_size, float input_scale,
+                                    int32_t input_zero_point,
+                                    int32_t weight_zero_point);
+
+/*
  * INT8 GEMV with a per-output-channel dequant epilogue:
  *   output[r] = (f32(acc[r]) * weight_scales[r]) * input_scale
  * where acc[r] is exactly ks_matvec_i8's int32 result; each product is one

@@ -67,6 +67,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [_vp, _vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _f, _i32, _i32],
     ),
+    "ks_b200_matvec_w4a8_f16_noalloc": (
+        c_int,
+        [_vp, _vp, _sz, _vp, _sz, _vp, _sz, _sz, _sz, _f, _i32, _i32],
+    ),
     "ks_b200_matvec_i8_dequant": (c_int, [_vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _i32, _i32]),
     "ks_b200_matvec_w4a8_async": (
         c_int,
