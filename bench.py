@@ -11,9 +11,11 @@ Workload (the W4A8 GEMV configuration of the headline metric):
 
   N > 1 GPUs (weak scaling): each rank holds an 11008-row shard of each of
   the 64 matrices ([N*11008, 4096] globally), runs the same per-GPU work as
-  N = 1, and the output slices are all-gathered over NVLink with NCCL in four
-  chunks of 16 GEMVs, each overlapped with the next chunk's GEMVs on a
-  second stream.
+  N = 1, and the output slices are gathered to every rank over NVLink: by
+  default the GEMV kernel itself stores each output into every rank's
+  gathered buffer (CUDA IPC peer pointers) and one arrival wait per step
+  closes it; `--gather nccl` uses NCCL all-gathers on a second stream
+  instead.
 
 Numbers:
   value      algorithmic bytes of all GEMVs of all ranks / device time (TB/s),
@@ -79,6 +81,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer e2e loop")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: output gather by peer stores from the GEMV kernel (default) or NCCL")
     return ap.parse_args()
 
 
@@ -186,11 +190,13 @@ def run_reference_arm(args):
     return 0
 
 
-def workload_config(world):
+def workload_config(world, gather="peer"):
     return {
         "workload": f"w4a8_gemv rows={ROWS} cols={COLS} group={GROUP} f16 scales; {MATS} resident matrices per step",
         "rows_per_gpu": ROWS, "cols": COLS, "group": GROUP, "scale_dtype": "f16", "gemvs_per_step": MATS,
-        "global_rows": ROWS * world, "parallelism": "row-shard + NCCL all-gather" if world > 1 else "single GPU",
+        "global_rows": ROWS * world,
+        "parallelism": ("row-shard + gather by peer stores (NVLink, CUDA IPC)" if gather == "peer" else
+                        "row-shard + NCCL all-gather") if world > 1 else "single GPU",
         "l2": f"inputs {MATS * gemv_bytes() / 1e9:.2f} GB per GPU > 126 MB L2; no flush",
         "bytes_per_gemv": gemv_bytes(),
     }
@@ -289,13 +295,24 @@ def run_b200_arm(args):
     main = torch.cuda.Stream(device=dev)
     comm = torch.cuda.Stream(device=dev)
     per_chunk = MATS // CHUNKS
+    peer = world > 1 and args.gather == "peer"
+    pgw = None
+    if peer:
+        from kernelsmith_b200.sharded import PeerGatherW4A8
+
+        pgw = PeerGatherW4A8(MATS, ROWS, dev)
+    signals = [0] * CHUNKS
 
     def gemv_chunk(c):
         # one batched launch: 16 independent GEMVs streamed back to back
         ms = range(c * per_chunk, (c + 1) * per_chunk)
-        K.matvec_w4a8_batch_async([X[m] for m in ms], [W[m] for m in ms], [S[m] for m in ms],
-                                  [Yloc[c, j] for j in range(per_chunk)], COLS // 2, COLS // GROUP, ROWS, COLS,
-                                  GROUP, SX, scale_type=K.SCALE_F16, status=status, stream=main)
+        if peer:
+            signals[c] = pgw.run([X[m] for m in ms], [W[m] for m in ms], [S[m] for m in ms], COLS, GROUP, SX,
+                                 K.SCALE_F16, stream=main, wait=False, m0=c * per_chunk)
+        else:
+            K.matvec_w4a8_batch_async([X[m] for m in ms], [W[m] for m in ms], [S[m] for m in ms],
+                                      [Yloc[c, j] for j in range(per_chunk)], COLS // 2, COLS // GROUP, ROWS,
+                                      COLS, GROUP, SX, scale_type=K.SCALE_F16, status=status, stream=main)
 
     def gemv_single_chain():
         # the same 64 GEMVs as 64 single launches (programmatic dependent launch chain)
@@ -308,49 +325,70 @@ def run_b200_arm(args):
     with torch.cuda.stream(main):
         for c in range(CHUNKS):
             gemv_chunk(c)  # warm-up / attribute setup outside capture
+        if peer:
+            pgw.wait(sum(signals), stream=main)
     main.synchronize()
     for c in range(CHUNKS):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=main):
             gemv_chunk(c)
         graphs.append(g)
+    wait_graph = None
+    if peer:
+        wait_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(wait_graph, stream=main):
+            pgw.wait(sum(signals), stream=main)
 
     def step():
         for c in range(CHUNKS):
             graphs[c].replay()
-            if world > 1:
+            if world > 1 and not peer:
                 ev = torch.cuda.Event()
                 ev.record(main)
                 comm.wait_event(ev)
                 with torch.cuda.stream(comm):
                     dist.all_gather_into_tensor(Yfull[c], Yloc[c])
-        if world > 1:
+        if peer:
+            wait_graph.replay()
+        elif world > 1:
             main.wait_stream(comm)
 
     with torch.cuda.stream(main):
         for _ in range(max(3, args.warmup)):
             step()
     torch.cuda.synchronize()
+    # NVML set-up and the sampling thread start before the ranks line up, so
+    # no rank enters the timed region late
+    clocks = ClockSampler(dev)
+    clocks.__enter__()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks, torch.cuda.stream(main):
-        start.record(main)
-        for _ in range(args.steps):
-            step()
-        end.record(main)
-        end.synchronize()
+    try:
+        with torch.cuda.stream(main):
+            start.record(main)
+            for _ in range(args.steps):
+                step()
+            end.record(main)
+            end.synchronize()
+    finally:
+        clocks.__exit__(None, None, None)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
+    rank_ms = [ms]
     if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        t = torch.zeros(world, device=dev)
+        t[rank] = ms
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        rank_ms = t.cpu().tolist()
+        ms = max(rank_ms)
         dist.barrier()
     st = status.cpu().tolist()
     assert st == [0, 0], f"device status {st}"
+    if peer:
+        pst = pgw.status.cpu().tolist()
+        assert pst == [0, 0], f"peer-gather status {pst}"
 
     # secondary: the single-GEMV launch chain (what a dependent decode chain of
     # ks_* calls costs per GEMV), timed the same way on this rank
@@ -394,13 +432,19 @@ def run_b200_arm(args):
     for g in graphs:
         del g
     graphs.clear()
+    wait_graph = None
+    if peer:
+        dist.barrier()
+        torch.cuda.synchronize()
+        pgw.close()
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "warmup": max(3, args.warmup), "ms_per_step": ms / args.steps,
+            "ms_per_step_by_rank": [round(v / args.steps, 5) for v in rank_ms], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "w4a8-i32acc-f32out",
             "data": "synthetic (seeded uniform int4 / int8, f16 scales U[1e-3,1e-2])",
-            "config": workload_config(world),
+            "config": workload_config(world, args.gather),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_GEMV, "traffic_per": "GEMV (ncu capture)",

@@ -184,6 +184,57 @@ int ks_b200_matvec_i8_batch_async(int count, const int8_t *const *inputs,
                                   void *stream);
 
 /*
+ * Multi-GPU row sharding (one process per GPU).  A weight matrix is split
+ * into contiguous row blocks, one per rank; each rank computes its rows and
+ * stores every output element straight into the gathered output buffer of
+ * every rank (peer memory over NVLink: plain stores, no multicast).  No
+ * collective library runs on the data path.
+ *
+ * ks_b200_ipc_get_handle / ks_b200_ipc_open_handle exchange device buffers
+ * between processes (CUDA IPC; `handle` is KS_B200_IPC_HANDLE_BYTES bytes,
+ * `offset` locates the buffer inside its allocation).
+ */
+#define KS_B200_IPC_HANDLE_BYTES 64
+int ks_b200_ipc_get_handle(const void *dev_ptr, unsigned char *handle,
+                           size_t *offset);
+int ks_b200_ipc_open_handle(const unsigned char *handle, size_t offset,
+                            void **peer_ptr);
+int ks_b200_ipc_close_handle(void *peer_ptr, size_t offset);
+
+/*
+ * Sharded batch: this rank's row block of `count` W4A8 matrices (rows x cols
+ * each, the shape of ks_b200_matvec_w4a8_batch_async).  The output of row r
+ * of matrix m is stored at rank_outputs[p][m * matrix_stride + row_offset + r]
+ * for every rank p (rank_outputs[p] is that rank's gathered buffer, opened
+ * with ks_b200_ipc_open_handle; this rank's own buffer included).  After its
+ * last store each CTA adds 1 to every rank's arrival counter
+ * (rank_counters[p]), behind a system-scope fence; *signals_per_rank
+ * receives how many such arrivals this call sends to each rank.  Needs the
+ * streaming kernel's shape rules (else KS_ERR_UNSUPPORTED).
+ */
+int ks_b200_matvec_w4a8_batch_gather_async(
+    int count, const int8_t *const *inputs,
+    const uint8_t *const *packed_weights, const void *const *weight_scales,
+    int nranks, float *const *rank_outputs, uint32_t *const *rank_counters,
+    size_t matrix_stride, size_t row_offset, size_t packed_stride_bytes,
+    int scale_type, size_t scale_stride, size_t rows, size_t cols,
+    size_t group_size, float input_scale, int32_t input_zero_point,
+    int32_t weight_zero_point, uint32_t *signals_per_rank, uint32_t *status,
+    void *stream);
+
+/*
+ * Queue a wait, on `stream`, until this rank's arrival counter has received
+ * `arrivals` more signals than at the previous wait (the running target is
+ * kept in expected[0], device memory initialised to 0 with the counter).
+ * With arrivals = nranks * signals_per_rank of the preceding sharded calls,
+ * the gathered outputs of all ranks are complete and visible once the wait
+ * returns.  The wait gives up after one second and sets status word 1.
+ */
+int ks_b200_peer_arrival_wait_async(const uint32_t *counter,
+                                    uint32_t *expected, uint32_t arrivals,
+                                    uint32_t *status, void *stream);
+
+/*
  * Skinny INT8 GEMM with requantisation (batched decode, M = 1..256 tokens):
  *   acc[m, n] = sum_k a[m, k] * w[n, k]                       (int32, exact)
  *   out[m, n] = sat_i8(rne(((f32(acc) * a_scales[m]) * w_scales[n]) / out_scale))

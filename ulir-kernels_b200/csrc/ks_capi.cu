@@ -10,6 +10,7 @@
 // There is no CPU fallback: if no CUDA device can run the kernels, compute
 // calls return KS_ERR_DEVICE.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -707,5 +708,112 @@ extern "C" int ks_b200_matvec_i8_batch_async(int count, const int8_t *const *inp
   GemvBatch b{count, inputs, reinterpret_cast<const void *const *>(weights),
               reinterpret_cast<const void *const *>(weight_scales), outputs};
   cudaError_t e = launch_i8_batch(a, b, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+// ============================================ multi-GPU: IPC and peer gather
+namespace {
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetAddressRangeFn>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+}  // namespace
+
+extern "C" int ks_b200_ipc_get_handle(const void *dev_ptr, unsigned char *handle, size_t *offset) {
+  if (!dev_ptr || !handle || !offset) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  Where w = classify(dev_ptr);
+  if (!w.device) return fail(KS_ERR_INVALID_ARG, "IPC handles need device memory");
+  cudaError_t e = cudaSetDevice(w.dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  GetAddressRangeFn range = address_range_fn();
+  if (!range) return fail(KS_ERR_DEVICE, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return fail(KS_ERR_DEVICE, "cuMemGetAddressRange failed");
+  cudaIpcMemHandle_t h;
+  if ((e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base))) != cudaSuccess)
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof h);
+  *offset = reinterpret_cast<uintptr_t>(dev_ptr) - static_cast<uintptr_t>(base);
+  return KS_OK;
+}
+
+extern "C" int ks_b200_ipc_open_handle(const unsigned char *handle, size_t offset, void **peer_ptr) {
+  if (!handle || !peer_ptr) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  void *base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *peer_ptr = static_cast<unsigned char *>(base) + offset;
+  return KS_OK;
+}
+
+extern "C" int ks_b200_ipc_close_handle(void *peer_ptr, size_t offset) {
+  if (!peer_ptr) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(static_cast<unsigned char *>(peer_ptr) - offset);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+extern "C" int ks_b200_matvec_w4a8_batch_gather_async(
+    int count, const int8_t *const *inputs, const uint8_t *const *packed_weights, const void *const *weight_scales,
+    int nranks, float *const *rank_outputs, uint32_t *const *rank_counters, size_t matrix_stride, size_t row_offset,
+    size_t packed_stride_bytes, int scale_type, size_t scale_stride, size_t rows, size_t cols, size_t group_size,
+    float input_scale, int32_t input_zero_point, int32_t weight_zero_point, uint32_t *signals_per_rank,
+    uint32_t *status, void *stream) {
+  if (!signals_per_rank) return fail(KS_ERR_INVALID_ARG, "NULL signals_per_rank");
+  *signals_per_rank = 0;
+  if (nranks < 1 || nranks > 8 || !rank_outputs || !rank_counters)
+    return fail(KS_ERR_INVALID_ARG, "nranks must be 1..8 with output and counter pointers per rank");
+  for (int p = 0; p < nranks; ++p)
+    if (!rank_outputs[p] || !rank_counters[p]) return fail(KS_ERR_INVALID_ARG, "NULL rank pointer");
+  if (row_offset + rows > matrix_stride) return fail(KS_ERR_INVALID_ARG, "row_offset + rows > matrix_stride");
+  if (count < 0 || (count > 0 && (!inputs || !packed_weights || !weight_scales)))
+    return fail(KS_ERR_INVALID_ARG, "bad batch arrays");
+  if (scale_type != kScaleF32 && scale_type != kScaleF16) return fail(KS_ERR_INVALID_ARG, "unknown scale_type");
+  for (int i = 0; i < count; ++i) {
+    int rc = w4a8_matvec_checks(inputs[i], packed_weights[i], packed_stride_bytes, weight_scales[i],
+                                scale_stride, rank_outputs[0], rows, cols, group_size, input_scale,
+                                input_zero_point, weight_zero_point);
+    if (rc != KS_OK) return rc;
+  }
+  if (count == 0) return KS_OK;
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  W4A8Launch a{};
+  a.wstride = (int64_t)packed_stride_bytes;
+  a.sstride = (int64_t)scale_stride;
+  a.stype = scale_type;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group_size;
+  a.sx = input_scale;
+  a.zx = input_zero_point;
+  a.zw = weight_zero_point;
+  a.status = status;
+  GemvBatch b{count, inputs, reinterpret_cast<const void *const *>(packed_weights), weight_scales, nullptr};
+  PeerGather pg{nranks, rank_outputs, rank_counters, (int64_t)matrix_stride, (int64_t)row_offset};
+  cudaError_t e = launch_w4a8_batch_gather(a, b, pg, static_cast<cudaStream_t>(stream), dev, signals_per_rank);
+  if (e == cudaErrorInvalidValue)
+    return fail(KS_ERR_UNSUPPORTED, "peer-gather GEMV needs the streaming kernel's shape and 16-byte alignment");
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_peer_arrival_wait_async(const uint32_t *counter, uint32_t *expected, uint32_t arrivals,
+                                               uint32_t *status, void *stream) {
+  if (!counter || !expected) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  cudaError_t e = launch_peer_wait(counter, expected, arrivals, status, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
 }

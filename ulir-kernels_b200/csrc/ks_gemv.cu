@@ -65,9 +65,36 @@ struct GemvItem {
   const uint8_t *s;  // scales (W4A8) or per-channel dequant scales (INT8 f32 out)
   void *y;
 };
+constexpr int kMaxPeers = 8;
+// Per-launch matrix list.  When npeers > 0 the launch is a sharded GEMV whose
+// outputs are gathered by peer stores: the output of row r of matrix m goes to
+// peer_y[p][m * mstride + row_offset + r] of every rank p (this rank
+// included), and after its last store each CTA adds 1 to every rank's
+// arrival counter peer_cnt[p] (system scope, after a system-scope fence).
 struct GemvItems {
   GemvItem it[kMaxItems];
+  float *peer_y[kMaxPeers];
+  uint32_t *peer_cnt[kMaxPeers];
+  int64_t mstride;
+  int64_t row_offset;
+  int32_t npeers;
 };
+
+// Where a row's result goes.
+struct OutRef {
+  void *y;               // local output (npeers == 0)
+  const GemvItems *items;
+  int64_t peer_off;      // m * mstride + row_offset
+};
+
+__device__ __forceinline__ void store_f32(const OutRef &o, int64_t r, float v) {
+  const int np = o.items->npeers;
+  if (np == 0) {
+    reinterpret_cast<float *>(o.y)[r] = v;
+  } else {
+    for (int p = 0; p < np; ++p) o.items->peer_y[p][o.peer_off + r] = v;
+  }
+}
 
 // Geometry of the streamed weight blocks, shared by all stream kernels.
 struct StreamGeom {
@@ -242,8 +269,8 @@ struct W4A8Op {
   // memory -> y.  Returns max(scale bits - 1) over the scales read.
   __device__ __forceinline__ static uint32_t rows2(const Params &p, const Lane &, const uint8_t *xb,
                                                    const uint8_t *wa, const uint8_t *sa, const uint8_t *wb,
-                                                   const uint8_t *sb, const GemvItem &it, int64_t ga, bool has_b,
-                                                   int lane) {
+                                                   const uint8_t *sb, const OutRef &out, const GemvItem &, int64_t ga,
+                                                   bool has_b, int lane) {
     float pa = 0.0f, pb = 0.0f;
     uint32_t mx = 0;
 #pragma unroll
@@ -266,9 +293,8 @@ struct W4A8Op {
       }
     }
     const float t = warp_sum_pair(pa, pb, lane);
-    float *y = reinterpret_cast<float *>(it.y);
-    if (lane == 0) y[ga] = t * p.sx;
-    if (lane == 16 && has_b) y[ga + 1] = t * p.sx;
+    if (lane == 0) store_f32(out, ga, t * p.sx);
+    if (lane == 16 && has_b) store_f32(out, ga + 1, t * p.sx);
     return mx;
   }
 
@@ -319,8 +345,8 @@ struct I8Op {
 
   __device__ __forceinline__ static uint32_t rows2(const Params &p, const Lane &L, const uint8_t *xb,
                                                    const uint8_t *wa, const uint8_t *, const uint8_t *wb,
-                                                   const uint8_t *, const GemvItem &it, int64_t ga, bool has_b,
-                                                   int lane) {
+                                                   const uint8_t *, const OutRef &, const GemvItem &it, int64_t ga,
+                                                   bool has_b, int lane) {
     const float *ws = reinterpret_cast<const float *>(it.s);
     float wsa = 0.0f, wsb = 0.0f;
     if (OUT_F32) {  // issue the per-channel scale loads early
@@ -476,13 +502,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
   uint32_t mx = 0;
   int gs = 0;
   int pair_base = 0;
-  bool stop = false;
-  for (int m = 0; m < g.count && !stop; ++m) {
+  bool stop = false;  // this warp hit a wait limit: it skips work but keeps every barrier
+  for (int m = 0; m < g.count; ++m) {
     const GemvItem &it = items.it[m];
+    const OutRef out{it.y, &items, (int64_t)m * items.mstride + items.row_offset};
     const uint8_t *xb = xbufs + (size_t)(m & 1) * g.xbuf_bytes;
     uint32_t pre[2][RW];
     const bool more = m + 1 < g.count;
-    if (more && prefetch) {
+    if (more && prefetch && !stop) {
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const int c = ctid + k * NT;
@@ -491,7 +518,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     }
     typename Op::Lane L;
     Op::lane_init(op, L, xb, lane);
-    for (int st = 0; st < nstages; ++st, ++gs) {
+    for (int st = 0; st < nstages && !stop; ++st, ++gs) {
       const int b = gs % g.nst;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[b], (uint32_t)(gs / g.nst) & 1u));
       if (!ok) {
@@ -511,31 +538,63 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         const int li = 2 * q;
         mx = max(mx, Op::rows2(op, L, xb, base + (size_t)li * g.row_bytes, sbase + (size_t)li * g.srow_bytes,
                                base + (size_t)(li + 1) * g.row_bytes, sbase + (size_t)(li + 1) * g.srow_bytes,
-                               it, r0 + lo + li, lo + li + 1 < hi, lane));
+                               out, it, r0 + lo + li, lo + li + 1 < hi, lane));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[b]);
     }
     pair_base += (rows_cta + 1) / 2;
-    if (more && !stop) {
-      uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
-      if (prefetch) {
+    if (more) {
+      if (!stop) {
+        uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
+        if (prefetch) {
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int c = ctid + k * NT;
-          if (c < op.chunks) Op::store_prep(op, pre[k], c, xn);
-        }
-      } else {
-        for (int c = ctid; c < op.chunks; c += NT) {
-          uint32_t raw[RW];
-          Op::load_raw(items.it[m + 1].x, c, g.x_al16 != 0, raw);
-          Op::store_prep(op, raw, c, xn);
+          for (int k = 0; k < 2; ++k) {
+            const int c = ctid + k * NT;
+            if (c < op.chunks) Op::store_prep(op, pre[k], c, xn);
+          }
+        } else {
+          for (int c = ctid; c < op.chunks; c += NT) {
+            uint32_t raw[RW];
+            Op::load_raw(items.it[m + 1].x, c, g.x_al16 != 0, raw);
+            Op::store_prep(op, raw, c, xn);
+          }
         }
       }
-      consumers_sync<CW>();
+      consumers_sync<CW>();  // every consumer warp, stopped or not, takes this barrier
     }
   }
   if (__any_sync(0xffffffffu, Op::bad(mx)) && lane == 0) set_status(g.status, kStatusBadScale);
+  if (items.npeers > 0) {
+    // all of this CTA's peer stores happen-before thread 0's system fence
+    consumers_sync<CW>();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < items.npeers; ++p)
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(items.peer_cnt[p]) : "memory");
+    }
+  }
+}
+
+// Waits until this rank's arrival counter reaches the running target: the
+// target (kept in expected[0]) grows by `arrivals` per call -- the number of
+// CTA signals the preceding sharded launches send to every rank.  Bounded by
+// the one-second wait limit; a timeout sets status word 1.
+__global__ void peer_arrival_wait_kernel(const uint32_t *counter, uint32_t *expected, uint32_t arrivals,
+                                         uint32_t *status) {
+  if (threadIdx.x != 0) return;
+  const uint32_t target = expected[0] + arrivals;
+  expected[0] = target;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    if ((int32_t)(v - target) >= 0) break;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      set_status(status, kStatusTimeout);
+      break;
+    }
+  }
 }
 
 // ------------------------------------------------------- generic kernels --
@@ -882,7 +941,7 @@ cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device) {
   W4A8Plan P;
   if (aligned16(a.w) && aligned16(a.s)) P = plan_w4a8(a, device, false);
   if (!P.fast) return launch_w4a8_generic(a, stream, device);
-  GemvItems items;
+  GemvItems items{};
   items.it[0] = GemvItem{a.x, a.w, reinterpret_cast<const uint8_t *>(a.s), a.y};
   P.g.count = 1;
   P.g.x_al16 = aligned16(a.x);
@@ -907,7 +966,7 @@ cudaError_t launch_w4a8_batch(const W4A8Launch &shape, const GemvBatch &b, cudaS
       }
       continue;
     }
-    GemvItems items;
+    GemvItems items{};
     for (int i = 0; i < n; ++i)
       items.it[i] = GemvItem{b.x[i0 + i], static_cast<const uint8_t *>(b.w[i0 + i]),
                              static_cast<const uint8_t *>(b.s[i0 + i]), b.y[i0 + i]};
@@ -925,7 +984,7 @@ cudaError_t launch_i8(const I8Launch &a, cudaStream_t stream, int device) {
   I8Plan P;
   if (aligned16(a.w)) P = plan_i8(a, device, false);
   if (!P.fast) return launch_i8_generic(a, stream, device);
-  GemvItems items;
+  GemvItems items{};
   items.it[0] = GemvItem{a.x, reinterpret_cast<const uint8_t *>(a.w), reinterpret_cast<const uint8_t *>(a.ws), a.y};
   P.g.count = 1;
   P.g.x_al16 = aligned16(a.x);
@@ -950,7 +1009,7 @@ cudaError_t launch_i8_batch(const I8Launch &shape, const GemvBatch &b, cudaStrea
       }
       continue;
     }
-    GemvItems items;
+    GemvItems items{};
     for (int i = 0; i < n; ++i)
       items.it[i] = GemvItem{b.x[i0 + i], static_cast<const uint8_t *>(b.w[i0 + i]),
                              static_cast<const uint8_t *>(b.s ? b.s[i0 + i] : nullptr), b.y[i0 + i]};
@@ -962,6 +1021,44 @@ cudaError_t launch_i8_batch(const I8Launch &shape, const GemvBatch &b, cudaStrea
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b, const PeerGather &pg,
+                                     cudaStream_t stream, int device, uint32_t *signals_per_rank) {
+  *signals_per_rank = 0;
+  if (pg.npeers < 1 || pg.npeers > kMaxPeers) return cudaErrorInvalidValue;
+  if (b.count <= 0) return cudaSuccess;
+  if (!batch_aligned(b, true)) return cudaErrorInvalidValue;
+  W4A8Plan P = plan_w4a8(shape, device, b.count > 1);
+  if (!P.fast) return cudaErrorInvalidValue;
+  for (int i0 = 0; i0 < b.count; i0 += kMaxItems) {
+    const int n = std::min(kMaxItems, b.count - i0);
+    GemvItems items{};
+    for (int i = 0; i < n; ++i)
+      items.it[i] = GemvItem{b.x[i0 + i], static_cast<const uint8_t *>(b.w[i0 + i]),
+                             static_cast<const uint8_t *>(b.s[i0 + i]), nullptr};
+    for (int p = 0; p < pg.npeers; ++p) {
+      items.peer_y[p] = pg.peer_y[p] + (int64_t)i0 * pg.mstride;
+      items.peer_cnt[p] = pg.peer_cnt[p];
+    }
+    items.npeers = pg.npeers;
+    items.mstride = pg.mstride;
+    items.row_offset = pg.row_offset;
+    W4A8Plan Q = P;
+    Q.g.count = n;
+    Q.g.x_al16 = batch_x_aligned(b, i0, n);
+    cudaError_t e = b.count > 1 ? launch_w4a8_cw<16>(Q, shape.stype, items, stream, device)
+                                : launch_w4a8_cw<8>(Q, shape.stype, items, stream, device);
+    if (e != cudaSuccess) return e;
+    *signals_per_rank += (uint32_t)Q.g.n_cta;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32_t arrivals, uint32_t *status,
+                             cudaStream_t stream) {
+  peer_arrival_wait_kernel<<<1, 32, 0, stream>>>(counter, expected, arrivals, status);
+  return cudaGetLastError();
 }
 
 }  // namespace ksb

@@ -85,6 +85,25 @@ struct GemvBatch {
 };
 cudaError_t launch_w4a8_batch(const W4A8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device);
 cudaError_t launch_i8_batch(const I8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device);
+
+// Sharded W4A8 batch whose outputs are gathered by peer stores (see the
+// kernel's GemvItems): the output of row r of matrix m is stored at
+// peer_y[p][m * mstride + row_offset + r] for every rank p, and every CTA of
+// every launch adds 1 to every rank's arrival counter.  signals_per_rank
+// receives how many arrivals this call sends to each rank.
+struct PeerGather {
+  int npeers;
+  float *const *peer_y;
+  uint32_t *const *peer_cnt;
+  int64_t mstride;
+  int64_t row_offset;
+};
+cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b, const PeerGather &pg,
+                                     cudaStream_t stream, int device, uint32_t *signals_per_rank);
+// Wait (bounded) until *counter reaches expected[0] + arrivals; expected[0]
+// then holds the new target.
+cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32_t arrivals, uint32_t *status,
+                             cudaStream_t stream);
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
 
 // Which kernel family launch_w4a8 / launch_i8 picked for a shape (tests and

@@ -33,6 +33,7 @@ SCALE_F16 = 1
 STATUS_WORDS = 2
 STATUS_BAD_SCALE = 0
 STATUS_TIMEOUT = 1
+IPC_HANDLE_BYTES = 64
 
 _vp = c_void_p
 _sz = c_size_t
@@ -86,6 +87,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, _vp, _vp, _vp, _vp, _sz, c_int, _sz, _sz, _sz, _sz, _f, _i32, _i32, _vp, _vp],
     ),
     "ks_b200_matvec_i8_batch_async": (c_int, [c_int, _vp, _vp, _vp, _vp, _sz, _sz, _sz, _i32, _i32, _f, _vp]),
+    "ks_b200_ipc_get_handle": (c_int, [_vp, _vp, _vp]),
+    "ks_b200_ipc_open_handle": (c_int, [_vp, _sz, _vp]),
+    "ks_b200_ipc_close_handle": (c_int, [_vp, _sz]),
+    "ks_b200_matvec_w4a8_batch_gather_async": (
+        c_int,
+        [c_int, _vp, _vp, _vp, c_int, _vp, _vp, _sz, _sz, _sz, c_int, _sz, _sz, _sz, _sz, _f, _i32, _i32, _vp,
+         _vp, _vp],
+    ),
+    "ks_b200_peer_arrival_wait_async": (c_int, [_vp, _vp, c_uint32, _vp, _vp]),
     "ks_b200_gemm_i8_requant": (c_int, [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz]),
     "ks_b200_gemm_i8_requant_async": (
         c_int,

@@ -15,6 +15,7 @@ asynchronous GEMV on the caller's stream.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable
 
@@ -104,3 +105,98 @@ def w4a8_compute_fn(x, w_shard, s_shard, cols: int, group: int, sx: float, scale
                             zx, zw, scale_type=scale_type, status=status, stream=stream)
 
     return run
+
+
+class PeerGatherW4A8:
+    """Sharded W4A8 batch whose outputs are gathered by peer stores over NVLink.
+
+    Every rank holds `rows` rows (its block) of each of up to `count` matrices
+    and a gathered buffer `y` of shape [count, world * rows]: after `run()` and
+    the arrival wait it queues, y[m] is the full output of matrix m on every
+    rank.  The buffers are exchanged once with CUDA IPC; the data path is the
+    GEMV kernel's own stores plus a one-thread arrival wait -- no collective
+    library.  Use two instances (or alternate buffers) when a consumer of y may
+    still be reading while the next run starts.
+
+    Create and close on every rank in the same order (the constructor runs one
+    all_gather_object on `group`).
+    """
+
+    def __init__(self, count: int, rows: int, device, group=None):
+        import torch
+        import torch.distributed as dist
+
+        import kernelsmith_b200 as K
+
+        self.K = K
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.count, self.rows = count, rows
+        self.y = torch.zeros((count, self.world * rows), dtype=torch.float32, device=device)
+        # word 0: arrival counter (written by every rank), word 1: wait target
+        self.sync = torch.zeros(2, dtype=torch.int32, device=device)
+        self.status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=device)
+        mine = []
+        for t in (self.y, self.sync):
+            h = (ctypes.c_ubyte * K.IPC_HANDLE_BYTES)()
+            off = ctypes.c_size_t()
+            K.check(K.lib().ks_b200_ipc_get_handle(t.data_ptr(), h, ctypes.byref(off)))
+            mine.append((bytes(h), off.value))
+        everyone = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(everyone, mine, group=group)
+        else:
+            everyone = [mine]
+        self._opened = []
+        y_ptrs, c_ptrs = [], []
+        for p in range(self.world):
+            if p == self.rank:
+                y_ptrs.append(self.y.data_ptr())
+                c_ptrs.append(self.sync.data_ptr())
+                continue
+            ptrs = []
+            for hb, off in everyone[p]:
+                out = ctypes.c_void_p()
+                K.check(K.lib().ks_b200_ipc_open_handle((ctypes.c_ubyte * len(hb)).from_buffer_copy(hb), off,
+                                                        ctypes.byref(out)))
+                self._opened.append((out.value, off))
+                ptrs.append(out.value)
+            y_ptrs.append(ptrs[0])
+            c_ptrs.append(ptrs[1])
+        self._y_ptrs = list(y_ptrs)
+        self._c_ptrs = (ctypes.c_void_p * self.world)(*c_ptrs)
+
+    def run(self, xs, ws, ss, cols, group, sx, scale_type, stream=None, w_stride=None, s_stride=None,
+            wait: bool = True, m0: int = 0) -> int:
+        """Queue this rank's GEMVs (gathered by peer stores into y[m0 : m0 + len(xs)])
+        and, if `wait`, the arrival wait.
+
+        Returns the signals each rank receives from this rank (the arrivals
+        to pass to wait() when several runs share one wait).
+        """
+        K = self.K
+        n = len(xs)
+        assert m0 + n <= self.count and len(ws) == len(ss) == n
+        sig = ctypes.c_uint32()
+        row_bytes = self.world * self.rows * 4
+        y_ptrs = (ctypes.c_void_p * self.world)(*[p + m0 * row_bytes for p in self._y_ptrs])
+        K.check(K.lib().ks_b200_matvec_w4a8_batch_gather_async(
+            n, K._ptr_array(xs), K._ptr_array(ws), K._ptr_array(ss), self.world, y_ptrs, self._c_ptrs,
+            self.world * self.rows, self.rank * self.rows, w_stride or cols // 2, scale_type,
+            s_stride or cols // group, self.rows, cols, group, sx, 0, 0,
+            ctypes.byref(sig), K.addr(self.status), K.stream_handle(stream)))
+        if wait:
+            self.wait(sig.value, stream)
+        return sig.value
+
+    def wait(self, signals_per_rank: int, stream=None) -> None:
+        """Queue the wait for every rank's signals of the preceding runs."""
+        K = self.K
+        K.check(K.lib().ks_b200_peer_arrival_wait_async(
+            self.sync.data_ptr(), self.sync.data_ptr() + 4, self.world * signals_per_rank,
+            K.addr(self.status), K.stream_handle(stream)))
+
+    def close(self) -> None:
+        for ptr, off in self._opened:
+            self.K.lib().ks_b200_ipc_close_handle(ptr, off)
+        self._opened = []
