@@ -81,6 +81,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer e2e loop")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-layers", type=int, default=32,
+                    help="secondary measurement: a chain of this many fused W4A8 decode layers (0: skip)")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N > 1: output gather by peer stores from the GEMV kernel (default) or NCCL")
     return ap.parse_args()
@@ -421,6 +423,8 @@ def run_b200_arm(args):
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(1, min(args.steps, 5))
     e2e = run_e2e(L, K, torch, dist, dev, world, rank, e2e_steps) if e2e_steps > 0 else None
 
+    layer = run_decode_layers(K, torch, dev, args) if args.decode_layers > 0 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n = MATS
@@ -454,6 +458,7 @@ def run_b200_arm(args):
             "single_launch_chain": {"us_per_gemv": chain_us, "GB_s": gemv_bytes() / chain_us / 1e3,
                                     "frac": gemv_bytes() / chain_us / 1e3 / peak,
                                     "note": "64 single-GEMV launches, PDL chain, per GPU"},
+            "decode_layer": layer,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": CHUNKS * args.steps * world,
@@ -464,6 +469,73 @@ def run_b200_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+LAYER_H, LAYER_I = 4096, 11008
+
+
+def layer_bytes(h=LAYER_H, i=LAYER_I, group=GROUP):
+    """Weights + f16 scales of one decode layer (QKV, O, gate, up, down)."""
+    mats = [(3 * h, h), (h, h), (i, h), (i, h), (h, i)]
+    return sum(r * c // 2 + r * (c // group) * 2 for r, c in mats)
+
+
+def run_decode_layers(K, torch, dev, args):
+    """A chain of fused W4A8 decode layers (hidden 4096, inter 11008, G 32,
+    distinct random weights per layer), graph-captured; per-layer time."""
+    import ctypes
+
+    L = K.lib()
+    n = args.decode_layers
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 17)
+    h, i = LAYER_H, LAYER_I
+    shapes = [(3 * h, h), (h, h), (i, h), (i, h), (h, i)]
+    Ws = [[torch.randint(0, 256, (r, c // 2), dtype=torch.uint8, device=dev, generator=gen) for r, c in shapes]
+          for _ in range(n)]
+    Ss = [[(torch.rand((r, c // GROUP), device=dev, generator=gen) * 9e-3 + 1e-3).to(torch.float16)
+           for r, c in shapes] for _ in range(n)]
+    norms = torch.rand((2, h), device=dev, generator=gen) + 0.5
+    acts = torch.zeros((n + 1, h), dtype=torch.float32, device=dev)
+    acts[0].uniform_(-1, 1, generator=gen)
+    ws_bytes = L.ks_b200_decode_layer_workspace(h, i)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
+    wp = [(ctypes.c_void_p * 5)(*[t.data_ptr() for t in W]) for W in Ws]
+    sp = [(ctypes.c_void_p * 5)(*[t.data_ptr() for t in S]) for S in Ss]
+    stream = torch.cuda.Stream(device=dev)
+
+    def chain():
+        for l in range(n):
+            K.check(L.ks_b200_decode_layer_w4a8_async(acts[l].data_ptr(), acts[l + 1].data_ptr(),
+                                                      norms[0].data_ptr(), norms[1].data_ptr(), 1e-5, wp[l], sp[l],
+                                                      h, i, GROUP, ws.data_ptr(), ws_bytes, status.data_ptr(),
+                                                      K.stream_handle(stream)))
+
+    with torch.cuda.stream(stream):
+        chain()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        chain()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * n)
+    del g
+    assert status.cpu().tolist() == [0, 0]
+    peak, _ = measured_hbm_peak()
+    b = layer_bytes()
+    return {"layers": n, "us_per_layer": us, "weight_bytes_per_layer": b, "GB_s": b / us / 1e3,
+            "frac": b / us / 1e3 / peak, "launches_per_layer": 4,
+            "shape": "hidden 4096, inter 11008, W4A8 G32 f16 scales, batch 1, fused RMSNorm/quantise/SiLU/residual"}
 
 
 def run_e2e(L, K, torch, dist, dev, world, rank, steps):

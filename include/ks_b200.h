@@ -235,6 +235,42 @@ int ks_b200_peer_arrival_wait_async(const uint32_t *counter,
                                     uint32_t *status, void *stream);
 
 /*
+ * One quantised Llama-style decode layer at batch 1 (no counterpart in the
+ * reference; it composes the reference's f32 RMSNorm, SiLU and multiply --
+ * ks_normalization.c:13-36, ks_activations.c:39-49, ks_elementwise.c:22-30 --
+ * with per-token int8 activation quantisation and four W4A8 GEMVs):
+ *   x1 = RMSNorm(h_in, norm1_w, eps)        q1, s1 = quantise(x1)
+ *   qkv = W_qkv [3h x h] . q1 * s1
+ *   v = qkv[2h : 3h]  (attention over one position returns V)
+ *                                           q2, s2 = quantise(v)
+ *   h2 = h_in + W_o [h x h] . q2 * s2
+ *   x3 = RMSNorm(h2, norm2_w, eps)          q3, s3 = quantise(x3)
+ *   gate = W_gate [i x h] . q3 * s3,  up = W_up [i x h] . q3 * s3
+ *   act = silu(gate) * up                   q4, s4 = quantise(act)
+ *   h_out = h2 + W_down [h x i] . q4 * s4
+ * quantise(v): s = max|v| / 127 (1 if v is all zero), q = sat_i8(rne(v / s)).
+ * weights[5] / scales_f16[5] are qkv, o, gate, up, down: packed int4 (row
+ * stride cols/2 bytes) with f16 group scales (row stride cols/group_size).
+ * Every step runs inside the four GEMV launches (activation preparation and
+ * epilogues are fused; the launches are chained with programmatic dependent
+ * launch).  `workspace` (device memory, ks_b200_decode_layer_workspace bytes)
+ * receives the intermediates, in this order, each region starting on a
+ * 256-byte boundary (ks_b200_decode_layer_offsets gives the 11 offsets and
+ * the total): f32 qkv[3h], h2[h], gate[i], up[i], act[i], s1..s4[4],
+ * u32 max|act| bits, int8 q1[h], q2[h], q3[h], q4[i].
+ */
+size_t ks_b200_decode_layer_workspace(size_t hidden, size_t inter);
+int ks_b200_decode_layer_offsets(size_t hidden, size_t inter, size_t *offsets);
+int ks_b200_decode_layer_w4a8_async(const float *h_in, float *h_out,
+                                    const float *norm1_w, const float *norm2_w,
+                                    float eps, const uint8_t *const *weights,
+                                    const uint16_t *const *scales_f16,
+                                    size_t hidden, size_t inter,
+                                    size_t group_size, void *workspace,
+                                    size_t workspace_bytes, uint32_t *status,
+                                    void *stream);
+
+/*
  * Skinny INT8 GEMM with requantisation (batched decode, M = 1..256 tokens):
  *   acc[m, n] = sum_k a[m, k] * w[n, k]                       (int32, exact)
  *   out[m, n] = sat_i8(rne(((f32(acc) * a_scales[m]) * w_scales[n]) / out_scale))

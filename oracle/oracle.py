@@ -232,3 +232,34 @@ def w4a8_tolerance_ok(y: np.ndarray, y_ref: np.ndarray, rel: float = 1e-4) -> tu
     ratio = np.abs(y - r) / bound
     worst = float(ratio.max()) if ratio.size else 0.0
     return worst <= 1.0, worst
+
+
+# ------------------------------------------------ decode layer (config 4) --
+def decode_layer_stages(orc: Oracle, h, norm1, norm2, eps, W, S16, hidden, inter, group):
+    """The quantised decode layer composed from the oracle's pieces, every
+    intermediate returned.  W[k] packed int4 rows, S16[k] f16 scale bits, for
+    k = qkv, o, gate, up, down (see include/ks_b200.h for the formulas)."""
+    out = {}
+
+    def gemv(k, q, s, rows, cols):
+        rc, y = orc.matvec_w4a8_f16(q, W[k], cols // 2, S16[k], cols // group, rows, cols, group, s)
+        assert rc == 0
+        return y
+
+    _, x1 = orc.rms_norm(h, norm1, eps)
+    _, out["q1"], out["s1"] = orc.quantize_per_token(x1)
+    out["qkv"] = gemv(0, out["q1"], out["s1"], 3 * hidden, hidden)
+    v = np.ascontiguousarray(out["qkv"][2 * hidden:])
+    _, out["q2"], out["s2"] = orc.quantize_per_token(v)
+    o = gemv(1, out["q2"], out["s2"], hidden, hidden)
+    out["h2"] = (h + o).astype(np.float32)
+    _, x3 = orc.rms_norm(out["h2"], norm2, eps)
+    _, out["q3"], out["s3"] = orc.quantize_per_token(x3)
+    out["gate"] = gemv(2, out["q3"], out["s3"], inter, hidden)
+    out["up"] = gemv(3, out["q3"], out["s3"], inter, hidden)
+    _, sg = orc.silu(out["gate"])
+    _, out["act"] = orc.mul(sg, out["up"])
+    _, out["q4"], out["s4"] = orc.quantize_per_token(out["act"])
+    d = gemv(4, out["q4"], out["s4"], hidden, inter)
+    out["h_out"] = (out["h2"] + d).astype(np.float32)
+    return out

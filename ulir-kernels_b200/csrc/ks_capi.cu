@@ -817,3 +817,81 @@ extern "C" int ks_b200_peer_arrival_wait_async(const uint32_t *counter, uint32_t
   cudaError_t e = launch_peer_wait(counter, expected, arrivals, status, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
 }
+
+// ================================================================ decode layer
+namespace {
+constexpr int kLayerRegions = 11;
+// f32 qkv[3h] | h2[h] | gate[i] | up[i] | act[i] | scales[4] | u32 amax[1] |
+// int8 q1[h] | q2[h] | q3[h] | q4[i], each region starting on a 256-byte boundary.
+void layer_offsets(size_t h, size_t i, size_t off[kLayerRegions + 1]) {
+  const size_t sizes[kLayerRegions] = {3 * h * 4, h * 4, i * 4, i * 4, i * 4, 16, 4, h, h, h, i};
+  size_t o = 0;
+  for (int r = 0; r < kLayerRegions; ++r) {
+    off[r] = o;
+    o += (sizes[r] + 255) / 256 * 256;
+  }
+  off[kLayerRegions] = o;
+}
+}  // namespace
+
+extern "C" size_t ks_b200_decode_layer_workspace(size_t hidden, size_t inter) {
+  size_t off[kLayerRegions + 1];
+  layer_offsets(hidden, inter, off);
+  return off[kLayerRegions];
+}
+
+extern "C" int ks_b200_decode_layer_offsets(size_t hidden, size_t inter, size_t *offsets) {
+  if (!offsets) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  size_t off[kLayerRegions + 1];
+  layer_offsets(hidden, inter, off);
+  for (int r = 0; r <= kLayerRegions; ++r) offsets[r] = off[r];
+  return KS_OK;
+}
+
+extern "C" int ks_b200_decode_layer_w4a8_async(const float *h_in, float *h_out, const float *norm1_w,
+                                               const float *norm2_w, float eps, const uint8_t *const *weights,
+                                               const uint16_t *const *scales_f16, size_t hidden, size_t inter,
+                                               size_t group_size, void *workspace, size_t workspace_bytes,
+                                               uint32_t *status, void *stream) {
+  if (!h_in || !h_out || !norm1_w || !norm2_w || !weights || !scales_f16 || !workspace)
+    return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  for (int k = 0; k < 5; ++k)
+    if (!weights[k] || !scales_f16[k]) return fail(KS_ERR_INVALID_ARG, "NULL weight or scale matrix");
+  if (!pos_finite(eps)) return fail(KS_ERR_INVALID_ARG, "eps must be > 0 and finite");
+  if (hidden == 0 || inter == 0 || hidden % 32 || inter % 32 || group_size < 32 || group_size % 32 ||
+      (group_size & (group_size - 1)) || hidden % group_size || inter % group_size)
+    return fail(KS_ERR_INVALID_ARG, "hidden and inter must be multiples of 32 and of group_size (a power of two >= 32)");
+  if (workspace_bytes < ks_b200_decode_layer_workspace(hidden, inter))
+    return fail(KS_ERR_WORKSPACE, "workspace smaller than ks_b200_decode_layer_workspace()");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  size_t off[kLayerRegions + 1];
+  layer_offsets(hidden, inter, off);
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  DecodeLayerArgs a{};
+  a.h_in = h_in;
+  a.h_out = h_out;
+  a.norm1_w = norm1_w;
+  a.norm2_w = norm2_w;
+  a.eps = eps;
+  for (int k = 0; k < 5; ++k) {
+    a.w[k] = weights[k];
+    a.s[k] = scales_f16[k];
+  }
+  a.hidden = (int64_t)hidden;
+  a.inter = (int64_t)inter;
+  a.group = (int64_t)group_size;
+  a.qkv = reinterpret_cast<float *>(ws + off[0]);
+  a.h2 = reinterpret_cast<float *>(ws + off[1]);
+  a.gate = reinterpret_cast<float *>(ws + off[2]);
+  a.up = reinterpret_cast<float *>(ws + off[3]);
+  a.act = reinterpret_cast<float *>(ws + off[4]);
+  a.scales = reinterpret_cast<float *>(ws + off[5]);
+  a.amax = reinterpret_cast<uint32_t *>(ws + off[6]);
+  for (int k = 0; k < 4; ++k) a.q[k] = reinterpret_cast<int8_t *>(ws + off[7 + k]);
+  a.status = status;
+  cudaError_t e = launch_decode_layer_w4a8(a, static_cast<cudaStream_t>(stream), dev);
+  if (e == cudaErrorInvalidValue)
+    return fail(KS_ERR_UNSUPPORTED, "decode layer needs 16-byte aligned weights/scales and the streaming shape");
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}

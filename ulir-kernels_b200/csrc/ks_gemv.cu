@@ -80,17 +80,58 @@ struct GemvItems {
   int32_t npeers;
 };
 
+// Decode-layer fusion: where a launch's activations come from and what its
+// epilogue does.  The zero-initialised value is the plain GEMV.
+enum XMode : int32_t {
+  kXInt8 = 0,     // int8 activations, scale from the arguments
+  kXF32 = 1,      // f32 activations, quantised per token (max |x| / 127, RNE)
+  kXRmsNorm = 2,  // f32 activations, RMSNorm (weight norm_w, eps), then quantised
+  kXF32Amax = 3,  // f32 activations quantised with the max |x| in *amax_in
+};
+enum EpiMode : int32_t {
+  kEpiPlain = 0,
+  kEpiResidual = 1,  // y[r] = v + res[r]
+  kEpiSiluMul = 2,   // matrix 1 of the launch: act[r] = silu(gate[r]) * v, max |act| into *amax_out
+};
+struct LayerExt {
+  int32_t xmode;
+  int32_t epi;
+  const float *xf;
+  const float *norm_w;
+  float eps;
+  const uint32_t *amax_in;
+  const float *res;
+  const float *gate;
+  float *act_out;
+  uint32_t *amax_out;
+  uint32_t *reset_amax;  // CTA 0 sets it to 0 after the wait (first launch of a layer)
+  int8_t *xq_out;        // optional: the quantised activations (written by CTA 0)
+  float *xs_out;         // optional: their scale
+};
+
 // Where a row's result goes.
 struct OutRef {
   void *y;               // local output (npeers == 0)
   const GemvItems *items;
   int64_t peer_off;      // m * mstride + row_offset
+  const LayerExt *ext;
+  int m;
 };
 
 __device__ __forceinline__ void store_f32(const OutRef &o, int64_t r, float v) {
   const int np = o.items->npeers;
   if (np == 0) {
-    reinterpret_cast<float *>(o.y)[r] = v;
+    const LayerExt &e = *o.ext;
+    float out = v;
+    if (e.epi == kEpiResidual) {
+      out = __fadd_rn(v, e.res[r]);
+    } else if (e.epi == kEpiSiluMul && o.m == 1) {
+      const float g = e.gate[r];
+      const float a = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), v);
+      e.act_out[r] = a;
+      atomicMax(e.amax_out, __float_as_uint(fabsf(a)));
+    }
+    reinterpret_cast<float *>(o.y)[r] = out;
   } else {
     for (int p = 0; p < np; ++p) o.items->peer_y[p][o.peer_off + r] = v;
   }
@@ -239,9 +280,18 @@ struct W4A8Op {
   using Params = W4A8OpParams;
   using SB = ScaleBits<ST>;
   static constexpr int kRawWords = 8;  // 32 activation bytes per chunk
-  struct Lane {};
+  static constexpr int kChunkK = 32;
+  __device__ __forceinline__ static void set_sx(const Params &p, uint8_t *xb, float sx) {
+    *reinterpret_cast<float *>(xb + 36 * p.chunks) = sx;
+  }
+  __device__ __forceinline__ static float default_sx(const Params &p) { return p.sx; }
+  struct Lane {
+    float sx;  // activation scale of the current matrix (from the prepared buffer)
+  };
 
-  static int xbuf_bytes(int chunks) { return ((chunks * 36 + 127) / 128) * 128; }
+  // 36 bytes per chunk, then the activation scale
+  static int xbuf_bytes(int chunks) { return ((chunks * 36 + 4 + 127) / 128) * 128; }
+
 
   __device__ __forceinline__ static void load_raw(const int8_t *x, int c, bool al16, uint32_t (&raw)[8]) {
     load_words<8>(x + 32 * c, al16, raw);
@@ -263,14 +313,16 @@ struct W4A8Op {
     reinterpret_cast<int *>(xb + 32 * p.chunks)[c] = (8 + p.zw) * (sumx - 32 * p.zx);
   }
 
-  __device__ __forceinline__ static void lane_init(const Params &, Lane &, const uint8_t *, int) {}
+  __device__ __forceinline__ static void lane_init(const Params &p, Lane &L, const uint8_t *xb, int) {
+    L.sx = *reinterpret_cast<const float *>(xb + 36 * p.chunks);
+  }
 
   // Two rows (b valid if has_b) whose weights and scale rows are in shared
   // memory -> y.  Returns max(scale bits - 1) over the scales read.
   __device__ __forceinline__ static uint32_t rows2(const Params &p, const Lane &, const uint8_t *xb,
                                                    const uint8_t *wa, const uint8_t *sa, const uint8_t *wb,
                                                    const uint8_t *sb, const OutRef &out, const GemvItem &, int64_t ga,
-                                                   bool has_b, int lane) {
+                                                   bool has_b, int lane, const Lane &Lx) {
     float pa = 0.0f, pb = 0.0f;
     uint32_t mx = 0;
 #pragma unroll
@@ -293,8 +345,8 @@ struct W4A8Op {
       }
     }
     const float t = warp_sum_pair(pa, pb, lane);
-    if (lane == 0) store_f32(out, ga, t * p.sx);
-    if (lane == 16 && has_b) store_f32(out, ga + 1, t * p.sx);
+    if (lane == 0) store_f32(out, ga, t * Lx.sx);
+    if (lane == 16 && has_b) store_f32(out, ga + 1, t * Lx.sx);
     return mx;
   }
 
@@ -314,6 +366,9 @@ template <int NCPL, bool OUT_F32, bool ZX>
 struct I8Op {
   using Params = I8OpParams;
   static constexpr int kRawWords = 4;
+  static constexpr int kChunkK = 16;
+  __device__ __forceinline__ static void set_sx(const Params &, uint8_t *, float) {}
+  __device__ __forceinline__ static float default_sx(const Params &p) { return p.sa; }
   struct Lane {
     int kl;  // sum of the chunk constants over this lane's chunks
   };
@@ -346,7 +401,7 @@ struct I8Op {
   __device__ __forceinline__ static uint32_t rows2(const Params &p, const Lane &L, const uint8_t *xb,
                                                    const uint8_t *wa, const uint8_t *, const uint8_t *wb,
                                                    const uint8_t *, const OutRef &, const GemvItem &it, int64_t ga,
-                                                   bool has_b, int lane) {
+                                                   bool has_b, int lane, const Lane &) {
     const float *ws = reinterpret_cast<const float *>(it.s);
     float wsa = 0.0f, wsb = 0.0f;
     if (OUT_F32) {  // issue the per-channel scale loads early
@@ -405,9 +460,101 @@ __device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
 }
 
+// Reductions over the consumer threads, in a fixed order (bitwise
+// reproducible).  `red` is CW floats of shared memory.
+template <int CW>
+__device__ __forceinline__ float consumers_sum(float v, float *red, int ctid) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((ctid & 31) == 0) red[ctid >> 5] = v;
+  consumers_sync<CW>();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < CW; ++w) t += red[w];
+  consumers_sync<CW>();
+  return t;
+}
+
+template <int CW>
+__device__ __forceinline__ float consumers_max(float v, float *red, int ctid) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((ctid & 31) == 0) red[ctid >> 5] = v;
+  consumers_sync<CW>();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < CW; ++w) t = fmaxf(t, red[w]);
+  consumers_sync<CW>();
+  return t;
+}
+
+__device__ __forceinline__ uint32_t quant_rne_byte(float v, float s) {
+  float q = rintf(__fdiv_rn(v, s));  // ties to even
+  q = fminf(fmaxf(q, -128.0f), 127.0f);
+  return (uint32_t)((int)q) & 0xFFu;
+}
+
+// Prepare matrix m's activations into buffer xb.  For f32 inputs every CTA
+// computes the same normalisation / scale from the whole vector, so no extra
+// kernel or global round trip is needed; the quantisation is
+//   s = max|v| / 127 (1 if the vector is all zero),  q = sat_i8(rne(v / s))
+// with v = x, or v = (x * rsqrt-scale) * norm_w for RMSNorm, where
+// rsqrt-scale = 1 / sqrtf(sum(x^2) / K + eps).  Contains consumer barriers:
+// every consumer warp must call it.
+template <class Op, int CW>
+__device__ void prep_x_f32(const typename Op::Params &op, const LayerExt &e, uint8_t *xb, float *red, int ctid) {
+  constexpr int NT = CW * 32;
+  const int chunks = op.chunks;
+  const int K = chunks * Op::kChunkK;
+  float scale = 1.0f;
+  if (e.xmode == kXRmsNorm) {
+    float ss = 0.0f;
+    for (int k = ctid; k < K; k += NT) {
+      const float v = e.xf[k];
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+    ss = consumers_sum<CW>(ss, red, ctid);
+    scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), e.eps)));
+  }
+  const bool rms = e.xmode == kXRmsNorm;
+  auto val = [&](int k) -> float {
+    const float v = e.xf[k];
+    return rms ? __fmul_rn(__fmul_rn(v, scale), e.norm_w[k]) : v;
+  };
+  float amax;
+  if (e.xmode == kXF32Amax) {
+    amax = __uint_as_float(*e.amax_in);
+  } else {
+    float m = 0.0f;
+    for (int k = ctid; k < K; k += NT) m = fmaxf(m, fabsf(val(k)));
+    amax = consumers_max<CW>(m, red, ctid);
+  }
+  const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  for (int c = ctid; c < chunks; c += NT) {
+    uint32_t raw[Op::kRawWords];
+#pragma unroll
+    for (int w = 0; w < Op::kRawWords; ++w) {
+      const int k = c * Op::kChunkK + 4 * w;
+      raw[w] = quant_rne_byte(val(k), s) | (quant_rne_byte(val(k + 1), s) << 8) |
+               (quant_rne_byte(val(k + 2), s) << 16) | (quant_rne_byte(val(k + 3), s) << 24);
+    }
+    Op::store_prep(op, raw, c, xb);
+    if (e.xq_out && blockIdx.x == 0) {
+#pragma unroll
+      for (int w = 0; w < Op::kRawWords; ++w)
+        reinterpret_cast<uint32_t *>(e.xq_out + (size_t)c * Op::kChunkK)[w] = raw[w];
+    }
+  }
+  if (ctid == 0) {
+    Op::set_sx(op, xb, s);
+    if (e.xs_out && blockIdx.x == 0) *e.xs_out = s;
+  }
+}
+
 template <class Op, int CW>
 __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
-    gemv_stream_kernel(const StreamGeom g, const typename Op::Params op, const GemvItems items) {
+    gemv_stream_kernel(const StreamGeom g, const typename Op::Params op, const GemvItems items,
+                       const LayerExt ext) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + g.nst;
@@ -491,21 +638,29 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
   const int ctid = threadIdx.x;
   constexpr int NT = CW * 32;
   constexpr int RW = Op::kRawWords;
-  for (int c = ctid; c < op.chunks; c += NT) {
-    uint32_t raw[RW];
-    Op::load_raw(items.it[0].x, c, g.x_al16 != 0, raw);
-    Op::store_prep(op, raw, c, xbufs);
+  float *red = reinterpret_cast<float *>(smem + kBarBytes - 128);  // CW <= 16 floats
+  if (ext.reset_amax && blockIdx.x == 0 && ctid == 0) *ext.reset_amax = 0u;
+  if (ext.xmode == kXInt8) {
+    for (int c = ctid; c < op.chunks; c += NT) {
+      uint32_t raw[RW];
+      Op::load_raw(items.it[0].x, c, g.x_al16 != 0, raw);
+      Op::store_prep(op, raw, c, xbufs);
+    }
+    if (ctid == 0) Op::set_sx(op, xbufs, Op::default_sx(op));
+  } else {
+    prep_x_f32<Op, CW>(op, ext, xbufs, red, ctid);
   }
   consumers_sync<CW>();
 
-  const bool prefetch = op.chunks <= 2 * NT;  // next matrix's raw x fits in registers
+  // next matrix's raw int8 x fits in registers
+  const bool prefetch = ext.xmode == kXInt8 && op.chunks <= 2 * NT;
   uint32_t mx = 0;
   int gs = 0;
   int pair_base = 0;
   bool stop = false;  // this warp hit a wait limit: it skips work but keeps every barrier
   for (int m = 0; m < g.count; ++m) {
     const GemvItem &it = items.it[m];
-    const OutRef out{it.y, &items, (int64_t)m * items.mstride + items.row_offset};
+    const OutRef out{it.y, &items, (int64_t)m * items.mstride + items.row_offset, &ext, m};
     const uint8_t *xb = xbufs + (size_t)(m & 1) * g.xbuf_bytes;
     uint32_t pre[2][RW];
     const bool more = m + 1 < g.count;
@@ -538,15 +693,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
         const int li = 2 * q;
         mx = max(mx, Op::rows2(op, L, xb, base + (size_t)li * g.row_bytes, sbase + (size_t)li * g.srow_bytes,
                                base + (size_t)(li + 1) * g.row_bytes, sbase + (size_t)(li + 1) * g.srow_bytes,
-                               out, it, r0 + lo + li, lo + li + 1 < hi, lane));
+                               out, it, r0 + lo + li, lo + li + 1 < hi, lane, L));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[b]);
     }
     pair_base += (rows_cta + 1) / 2;
     if (more) {
-      if (!stop) {
-        uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
+      uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
+      if (ext.xmode != kXInt8) {
+        prep_x_f32<Op, CW>(op, ext, xn, red, ctid);  // has barriers: every warp calls it
+      } else if (!stop) {
+        if (ctid == 0) Op::set_sx(op, xn, Op::default_sx(op));
         if (prefetch) {
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
@@ -716,7 +874,7 @@ bool pdl_enabled(cudaStream_t stream) {
 
 template <class Op, int CW>
 cudaError_t launch_stream(const StreamGeom &g, const typename Op::Params &op, const GemvItems &items,
-                          cudaStream_t stream, int dev) {
+                          cudaStream_t stream, int dev, const LayerExt &ext = LayerExt{}) {
   static std::once_flag attr_once[64];
   static cudaError_t attr_err[64];
   std::call_once(attr_once[dev & 63], [&] {
@@ -737,7 +895,7 @@ cudaError_t launch_stream(const StreamGeom &g, const typename Op::Params &op, co
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<Op, CW>, g, op, items);
+  return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<Op, CW>, g, op, items, ext);
 }
 
 int ncpl_of(int chunks) {
@@ -766,7 +924,7 @@ W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch) {
   const int ssize = a.stype == kScaleF16 ? 2 : 4;
   const int64_t groups = (a.cols + a.group - 1) / a.group;
   const int chunks = (int)(a.cols / 32);
-  const int xbuf = ((chunks * 36 + 127) / 128) * 128;
+  const int xbuf = ((chunks * 36 + 4 + 127) / 128) * 128;
   StreamGeom g{};
   if (!plan_stream(g, a.rows, (int)(a.cols / 2), (int)(groups * ssize), xbuf, device_props(device).sm_count,
                    batch, batch ? 16 : 8))
@@ -788,24 +946,26 @@ W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch) {
 }
 
 template <typename ST, bool ZX, int CW>
-cudaError_t launch_w4a8_ncpl(const W4A8Plan &P, const GemvItems &items, cudaStream_t stream, int dev) {
+cudaError_t launch_w4a8_ncpl(const W4A8Plan &P, const GemvItems &items, cudaStream_t stream, int dev,
+                             const LayerExt &ext) {
   switch (P.ncpl) {
-    case 1: return launch_stream<W4A8Op<ST, 1, ZX>, CW>(P.g, P.op, items, stream, dev);
-    case 2: return launch_stream<W4A8Op<ST, 2, ZX>, CW>(P.g, P.op, items, stream, dev);
-    case 4: return launch_stream<W4A8Op<ST, 4, ZX>, CW>(P.g, P.op, items, stream, dev);
-    case 8: return launch_stream<W4A8Op<ST, 8, ZX>, CW>(P.g, P.op, items, stream, dev);
-    default: return launch_stream<W4A8Op<ST, 16, ZX>, CW>(P.g, P.op, items, stream, dev);
+    case 1: return launch_stream<W4A8Op<ST, 1, ZX>, CW>(P.g, P.op, items, stream, dev, ext);
+    case 2: return launch_stream<W4A8Op<ST, 2, ZX>, CW>(P.g, P.op, items, stream, dev, ext);
+    case 4: return launch_stream<W4A8Op<ST, 4, ZX>, CW>(P.g, P.op, items, stream, dev, ext);
+    case 8: return launch_stream<W4A8Op<ST, 8, ZX>, CW>(P.g, P.op, items, stream, dev, ext);
+    default: return launch_stream<W4A8Op<ST, 16, ZX>, CW>(P.g, P.op, items, stream, dev, ext);
   }
 }
 
 template <int CW>
-cudaError_t launch_w4a8_cw(const W4A8Plan &P, int stype, const GemvItems &items, cudaStream_t stream, int dev) {
+cudaError_t launch_w4a8_cw(const W4A8Plan &P, int stype, const GemvItems &items, cudaStream_t stream, int dev,
+                           const LayerExt &ext = LayerExt{}) {
   const bool zx = P.op.zx != 0;
   if (stype == kScaleF16)
-    return zx ? launch_w4a8_ncpl<__half, true, CW>(P, items, stream, dev)
-              : launch_w4a8_ncpl<__half, false, CW>(P, items, stream, dev);
-  return zx ? launch_w4a8_ncpl<float, true, CW>(P, items, stream, dev)
-            : launch_w4a8_ncpl<float, false, CW>(P, items, stream, dev);
+    return zx ? launch_w4a8_ncpl<__half, true, CW>(P, items, stream, dev, ext)
+              : launch_w4a8_ncpl<__half, false, CW>(P, items, stream, dev, ext);
+  return zx ? launch_w4a8_ncpl<float, true, CW>(P, items, stream, dev, ext)
+            : launch_w4a8_ncpl<float, false, CW>(P, items, stream, dev, ext);
 }
 
 // ---- INT8 ---------------------------------------------------------------
@@ -1059,6 +1219,75 @@ cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32
                              cudaStream_t stream) {
   peer_arrival_wait_kernel<<<1, 32, 0, stream>>>(counter, expected, arrivals, status);
   return cudaGetLastError();
+}
+
+// One quantised decode layer (batch 1): four chained launches of the
+// streaming W4A8 kernel with fused activation preparation and epilogues.
+//   1  qkv  = W_qkv . q(RMSNorm(h_in, norm1))            (RMSNorm + quantise in the prologue)
+//   2  h2   = h_in + W_o . q(qkv[2h:3h])                  (attention at one position is V)
+//   3  gate = W_g . q(RMSNorm(h2, norm2)), up = W_u . (same); act = silu(gate) * up, max|act|
+//   4  h_out = h2 + W_d . q(act)                          (scale from max|act|)
+cudaError_t launch_decode_layer_w4a8(const DecodeLayerArgs &a, cudaStream_t stream, int device) {
+  const int64_t h = a.hidden, i = a.inter;
+  struct Stage {
+    int64_t rows, cols;
+    int count;
+    const uint8_t *w[2];
+    const void *s[2];
+    float *y[2];
+    LayerExt ext;
+  } st[4] = {};
+  st[0] = {3 * h, h, 1, {a.w[0]}, {a.s[0]}, {a.qkv}, LayerExt{}};
+  st[0].ext.xmode = kXRmsNorm;
+  st[0].ext.xf = a.h_in;
+  st[0].ext.norm_w = a.norm1_w;
+  st[0].ext.eps = a.eps;
+  st[0].ext.reset_amax = a.amax;
+  st[1] = {h, h, 1, {a.w[1]}, {a.s[1]}, {a.h2}, LayerExt{}};
+  st[1].ext.xmode = kXF32;
+  st[1].ext.xf = a.qkv + 2 * h;
+  st[1].ext.epi = kEpiResidual;
+  st[1].ext.res = a.h_in;
+  st[2] = {i, h, 2, {a.w[2], a.w[3]}, {a.s[2], a.s[3]}, {a.gate, a.up}, LayerExt{}};
+  st[2].ext.xmode = kXRmsNorm;
+  st[2].ext.xf = a.h2;
+  st[2].ext.norm_w = a.norm2_w;
+  st[2].ext.eps = a.eps;
+  st[2].ext.epi = kEpiSiluMul;
+  st[2].ext.gate = a.gate;
+  st[2].ext.act_out = a.act;
+  st[2].ext.amax_out = a.amax;
+  st[3] = {h, i, 1, {a.w[4]}, {a.s[4]}, {a.h_out}, LayerExt{}};
+  st[3].ext.xmode = kXF32Amax;
+  st[3].ext.xf = a.act;
+  st[3].ext.amax_in = a.amax;
+  st[3].ext.epi = kEpiResidual;
+  st[3].ext.res = a.h2;
+  for (int k = 0; k < 4; ++k) {
+    Stage &S = st[k];
+    S.ext.xq_out = a.q[k];
+    S.ext.xs_out = a.scales + k;
+    W4A8Launch shape{};
+    shape.wstride = S.cols / 2;
+    shape.sstride = S.cols / a.group;
+    shape.stype = kScaleF16;
+    shape.rows = S.rows;
+    shape.cols = S.cols;
+    shape.group = a.group;
+    shape.sx = 1.0f;
+    shape.status = a.status;
+    for (int m = 0; m < S.count; ++m)
+      if (!aligned16(S.w[m]) || !aligned16(S.s[m])) return cudaErrorInvalidValue;
+    W4A8Plan P = plan_w4a8(shape, device, false);
+    if (!P.fast) return cudaErrorInvalidValue;
+    GemvItems items{};
+    for (int m = 0; m < S.count; ++m) items.it[m] = GemvItem{nullptr, S.w[m], static_cast<const uint8_t *>(S.s[m]), S.y[m]};
+    P.g.count = S.count;
+    P.g.x_al16 = 1;
+    cudaError_t e = launch_w4a8_cw<8>(P, kScaleF16, items, stream, device, S.ext);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace ksb

@@ -100,6 +100,25 @@ struct PeerGather {
 };
 cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b, const PeerGather &pg,
                                      cudaStream_t stream, int device, uint32_t *signals_per_rank);
+// One quantised decode layer (see launch_decode_layer_w4a8 in ks_gemv.cu).
+// w/s: qkv [3h x h], o [h x h], gate [i x h], up [i x h], down [h x i], W4A8
+// with f16 group scales, dense strides.  The other pointers are the caller's
+// workspace regions (ks_b200_decode_layer_workspace).
+struct DecodeLayerArgs {
+  const float *h_in;
+  float *h_out;
+  const float *norm1_w, *norm2_w;
+  float eps;
+  const uint8_t *w[5];
+  const void *s[5];
+  int64_t hidden, inter, group;
+  float *qkv, *h2, *gate, *up, *act, *scales;
+  uint32_t *amax;
+  int8_t *q[4];
+  uint32_t *status;
+};
+cudaError_t launch_decode_layer_w4a8(const DecodeLayerArgs &a, cudaStream_t stream, int device);
+
 // Wait (bounded) until *counter reaches expected[0] + arrivals; expected[0]
 // then holds the new target.
 cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32_t arrivals, uint32_t *status,

@@ -96,6 +96,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _vp, _vp],
     ),
     "ks_b200_peer_arrival_wait_async": (c_int, [_vp, _vp, c_uint32, _vp, _vp]),
+    "ks_b200_decode_layer_workspace": (_sz, [_sz, _sz]),
+    "ks_b200_decode_layer_offsets": (c_int, [_sz, _sz, _vp]),
+    "ks_b200_decode_layer_w4a8_async": (
+        c_int,
+        [_vp, _vp, _vp, _vp, _f, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _vp, _vp],
+    ),
     "ks_b200_gemm_i8_requant": (c_int, [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz]),
     "ks_b200_gemm_i8_requant_async": (
         c_int,
