@@ -128,3 +128,63 @@ def test_gemm_rejects_bad_args(ks):
                                      8) == E
     assert L.ks_b200_gemm_i8_requant(None, 8, ks.addr(s), ks.addr(a), 8, ks.addr(s), 1.0, ks.addr(o), 4, 2, 4,
                                      8) == E
+
+
+def test_gemm_chain_on_side_stream(ks, cuda, oracle):
+    """Three GEMMs queued back to back on a non-default stream (programmatic
+    dependent launch on), each one's int8 output the next one's activations:
+    every stage must equal the oracle chain bit for bit, so no CTA may read its
+    activations or scales before the previous grid has finished."""
+    import torch
+
+    m, k = 16, 4096
+    g = np.random.default_rng(123)
+    a0 = g.integers(-127, 128, (m, k), dtype=np.int8)
+    ws_list = [g.integers(-127, 128, (k, k), dtype=np.int8) for _ in range(3)]
+    sws = [g.uniform(1e-3, 1e-2, k).astype(np.float32) for _ in range(3)]
+    sa = np.full(m, 1.1e-3, np.float32)  # keeps every stage's outputs mostly unsaturated
+    out_scale = 0.05
+    stream = torch.cuda.Stream(device=cuda)
+    dev = lambda x: torch.from_numpy(x).to(cuda)
+    da, dsa = dev(a0), dev(sa)
+    dws, dsws = [dev(w) for w in ws_list], [dev(s) for s in sws]
+    outs = [torch.zeros((m, k), dtype=torch.int8, device=cuda) for _ in range(3)]
+    status = torch.zeros(2, dtype=torch.int32, device=cuda)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        src = da
+        for i in range(3):
+            ks.gemm_i8_requant_async(src, dsa, dws[i], dsws[i], out_scale, outs[i], m, k, k, status=status,
+                                     stream=stream)
+            src = outs[i]
+    stream.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    ref = a0
+    for i in range(3):
+        rc, ref = oracle.gemm_i8_requant(ref, sa, ws_list[i], sws[i], out_scale)
+        assert rc == 0
+        got = outs[i].cpu().numpy()
+        np.testing.assert_array_equal(got, ref)
+        assert len(np.unique(ref)) > 20  # the chain carries information
+
+
+@pytest.mark.parametrize("out_scale", [2.0, 6.0, 0.4])
+def test_gemm_requant_exact_ties(ks, cuda, oracle, out_scale):
+    """Unit scales and small integers make t = acc exactly, so acc / out_scale
+    (rounded to f32) falls exactly on half-integers (round half to even) for
+    many outputs, and 1 / 6 and 1 / 0.4 are not exact in f32: the
+    division-free epilogue must still agree with the divided result everywhere."""
+    import torch
+
+    m, n, k = 16, 640, 64
+    g = np.random.default_rng(int(out_scale * 8))
+    a = g.integers(-3, 4, (m, k), dtype=np.int8)
+    w = g.integers(-3, 4, (n, k), dtype=np.int8)
+    sa = np.ones(m, np.float32)
+    ws = np.ones(n, np.float32)
+    out, acc = _run_async(ks, torch, cuda, a, w, sa, ws, out_scale)
+    rc, out_ref, acc_ref = oracle.gemm_i8_requant(a, sa, w, ws, out_scale, want_acc=True)
+    np.testing.assert_array_equal(acc, acc_ref)
+    np.testing.assert_array_equal(out, out_ref)
+    q = acc_ref.astype(np.float32) / np.float32(out_scale)
+    assert (q - np.floor(q) == np.float32(0.5)).sum() > 100  # exact ties are present

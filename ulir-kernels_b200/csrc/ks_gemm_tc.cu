@@ -10,17 +10,30 @@
 // its N dimension (padded to a multiple of 16), so a [128 x Mpad] int32 tile
 // lives in TMEM while all of K streams through shared memory.
 //
-// One CTA per 128 weight rows, warp-specialised:
+// Every SM gets the same share of weight rows: a CTA owns `tile_rows` =
+// ceil(N / (waves * SMs * ctas_per_SM)) consecutive rows (at most 128; the
+// TMA box height), so the weight stream -- the bound at M <= 64 -- is spread
+// over all SMs instead of over ceil(N / 128) CTAs.  The MMA is always
+// M = 128; accumulator lanes at and above tile_rows belong to no weight row
+// of the CTA and are never stored.
+//
+// Warp-specialised CTA of 192 threads:
 //   warp 0  TMA producer: per 128-byte K block, one 2-D tiled copy of the
-//           weight tile [128 x 128 B] and one of the activation tile
+//           weight tile [tile_rows x 128 B] and one of the activation tile
 //           [Mpad x 128 B], both 128-byte swizzled, into a ring of stages.
-//           No multicast anywhere.
+//           The weight copies of the first stages are issued before
+//           griddepcontrol.wait (weights are never written by the kernels of
+//           this library that trigger an early launch); the activations only
+//           after it.  No multicast anywhere.
 //   warp 1  allocates TMEM, issues 4 x tcgen05.mma (K = 32 each) per stage,
 //           frees the stage with tcgen05.commit, finally commits to the
 //           accumulator barrier; deallocates TMEM at the end.
-//   warps 2-5 epilogue: tcgen05.ld the accumulator rows (one TMEM lane per
-//           weight row), requantise in the order written above with IEEE
-//           round-to-nearest operations and store int8.
+//   warps 2-5 epilogue: after griddepcontrol.wait, stage the per-token
+//           activation scales in shared memory and the row's weight scale in
+//           a register while the main loop runs; then tcgen05.ld the
+//           accumulator rows (one TMEM lane per weight row), requantise in the
+//           order written above with IEEE round-to-nearest operations and
+//           store int8.
 //
 // Every mbarrier wait is bounded (about one second); on a timeout the kernel
 // records it in the status word, lets in-flight copies and MMAs drain, frees
@@ -30,7 +43,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "ks_internal.h"
@@ -40,27 +55,53 @@ namespace ksb {
 
 namespace {
 
-constexpr int kTileRows = 128;   // weight rows per CTA (MMA M)
+constexpr int kMmaRows = 128;    // MMA M = TMEM lanes; a CTA stores its first tile_rows
 constexpr int kKBlock = 128;     // K bytes per stage (one 128-B swizzle row)
 constexpr int kGemmThreads = 192;
+constexpr int kEpiThreads = 128;  // warps 2-5
 constexpr int kMaxTokens = 256;  // MMA N limit
+constexpr int kMaxStages = 12;
+constexpr int kWTileBytes = kMmaRows * kKBlock;  // weight region of a stage (MMA reads 128 rows)
+constexpr int kBarRegion = 1024;                 // barriers, TMEM slot, abort flag
+constexpr int kScaleRegion = kMaxTokens * 4;     // activation scales
 
 struct GemmParams {
   const float *sa;
   const float *ws;
   float out_scale;
+  float inv_out_scale;  // RN(1 / out_scale), or 0 when that is not finite (then divide)
   int8_t *out;
   int64_t ldo;
   int32_t *acc_out;  // optional
   int32_t m, n, k;
-  int32_t mpad;      // tokens padded to a multiple of 16
-  int32_t nkb;       // K blocks
-  int32_t nst;       // stages
+  int32_t mpad;       // tokens padded to a multiple of 16
+  int32_t nkb;        // K blocks
+  int32_t nst;        // stages
   int32_t stage_bytes;
-  int32_t b_bytes;   // activation tile bytes per stage
+  int32_t b_bytes;    // activation tile bytes per stage
+  int32_t tile_rows;  // weight rows per CTA (TMA box height, multiple of 16, <= 128)
+  int32_t tma_store;  // 1: the int8 tile leaves through one TMA store (aligned out, ldo)
   uint32_t tmem_cols;
   uint32_t *status;
 };
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void epi_barrier() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
+// AND of `pred` over the epilogue warps (named barrier 1): every epilogue
+// thread takes the same branch after it, so none can miss a later barrier.
+__device__ __forceinline__ bool epi_all(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(kEpiThreads)
+      : "memory");
+  return r != 0;
+}
 
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
   asm volatile(
@@ -115,16 +156,6 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 __device__ __forceinline__ int8_t requant(int32_t acc, float sa, float ws, float out_scale) {
   float t = __fmul_rn((float)acc, sa);
   t = __fmul_rn(t, ws);
@@ -134,9 +165,77 @@ __device__ __forceinline__ int8_t requant(int32_t acc, float sa, float ws, float
   return (int8_t)(int)t;
 }
 
+__device__ __forceinline__ void tc_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Wait for the preceding tcgen05.ld; the registers pass through the asm so no
+// use of them can be scheduled before the wait.
+__device__ __forceinline__ void tc_wait_ld(uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                 "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]),
+                 "+r"(a[15]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]),
+                 "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]),
+                 "+r"(b[14]), "+r"(b[15])
+               :
+               : "memory");
+}
+
+// Sixteen requant() results without a division per element and without a
+// branch per element, so the sixteen chains overlap.  inv = RN(1/out_scale)
+// (finite).  q = RN(t * inv) and the correctly rounded quotient RN(t/out_scale)
+// both lie within |t/out_scale| * 2^-23 of the exact quotient (two and one
+// half-ulp errors), i.e. within 3.1e-5 while |q| < 129; rint() can tell them
+// apart only across a half-integer.  q is clamped to [-129, 128] (fmaxf maps
+// NaN to -129, like fmaxf(NaN, -128) in requant()); y = RN(q + 1.5 * 2^23)
+// holds rint(q) (ties to even) in its low mantissa bits, r = y - 1.5 * 2^23 is
+// the same integer as a float, and |q - r| within 2^-14 of 0.5 marks a
+// near-tie.  Only near-ties (rare; one warp-uniform test per 16) divide.
+__device__ __forceinline__ void requant16(const uint32_t (&v)[16], const float *sv, float ws, float out_scale,
+                                          float inv, int (&o)[16]) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr int kMagicBits = 0x4B400000;
+  float t[16];
+  uint32_t near = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    t[j] = __fmul_rn(__fmul_rn((float)(int32_t)v[j], sv[j]), ws);
+    const float q = fminf(fmaxf(__fmul_rn(t[j], inv), -129.0f), 128.0f);
+    const float y = __fadd_rn(q, kMagic);
+    const float r = __fsub_rn(y, kMagic);
+    near |= (__fsub_rn(0.5f, fabsf(__fsub_rn(q, r))) < 0x1p-14f ? 1u : 0u) << j;
+    o[j] = __float_as_int(y) - kMagicBits;
+  }
+  if (__any_sync(0xffffffffu, near != 0)) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if ((near >> j) & 1u) {
+        float e = rintf(__fdiv_rn(t[j], out_scale));
+        o[j] = (int)fminf(fmaxf(e, -128.0f), 127.0f);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j] = min(max(o[j], -128), 127);
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+               "r"(y), "r"(smem_u32(src))
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_i8_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
-                      const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmap_out, const GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -146,10 +245,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *accum = empty + p.nst;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accum + 1);
   volatile uint32_t *abort_flag = tmem_slot + 1;
+  float *sa_s = reinterpret_cast<float *>(smem + (size_t)p.nst * p.stage_bytes + kBarRegion);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kTileRows;
+  const int row0 = blockIdx.x * p.tile_rows;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.nst; ++s) {
@@ -177,11 +277,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_a);
       const uint64_t pol = l2_policy_evict_first();
-      const uint32_t tx = (uint32_t)(kTileRows * kKBlock + p.b_bytes);
-      int issued = 0;
-      for (int kb = 0; kb < p.nkb; ++kb) {
+      const uint32_t tx = (uint32_t)(p.tile_rows * kKBlock + p.b_bytes);
+      const int pre = min(p.nst, p.nkb);
+      // weights of the first stages, before the previous grid has finished
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], tx);
+        tma_load_2d_hint(stages + (size_t)kb * p.stage_bytes, &tmap_w, kb * kKBlock, row0, &full[kb], pol);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int kb = 0; kb < pre; ++kb)
+        tma_load_2d(stages + (size_t)kb * p.stage_bytes + kWTileBytes, &tmap_a, kb * kKBlock, 0, &full[kb]);
+      int issued = pre;
+      for (int kb = pre; kb < p.nkb; ++kb) {
         const int s = kb % p.nst;
-        if (kb >= p.nst && !mbar_wait(&empty[s], (uint32_t)((kb / p.nst) - 1) & 1u)) {
+        if (!mbar_wait(&empty[s], (uint32_t)((kb / p.nst) - 1) & 1u)) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
@@ -189,7 +299,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
         mbar_arrive_expect_tx(&full[s], tx);
         tma_load_2d_hint(st, &tmap_w, kb * kKBlock, row0, &full[s], pol);
-        tma_load_2d(st + kTileRows * kKBlock, &tmap_a, kb * kKBlock, 0, &full[s]);
+        tma_load_2d(st + kWTileBytes, &tmap_a, kb * kKBlock, 0, &full[s]);
         ++issued;
       }
       for (int kb = max(0, issued - p.nst); kb < issued; ++kb) {
@@ -202,7 +312,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc = (2u << 4)                         // D: s32
                              | (1u << 7) | (1u << 10)          // A, B: signed int8
                              | ((uint32_t)(p.mpad >> 3) << 17) // N
-                             | ((uint32_t)(kTileRows >> 4) << 24);  // M
+                             | ((uint32_t)(kMmaRows >> 4) << 24);  // M
       for (int kb = 0; kb < p.nkb; ++kb) {
         const int s = kb % p.nst;
         if (!mbar_wait(&full[s], (uint32_t)(kb / p.nst) & 1u)) {
@@ -213,7 +323,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
         const uint64_t adesc = umma_desc_sw128(st);
-        const uint64_t bdesc = umma_desc_sw128(st + kTileRows * kKBlock);
+        const uint64_t bdesc = umma_desc_sw128(st + kWTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kKBlock / 32; ++kk) {
           // advance the start address by 32 bytes (K = 32 int8) per step
@@ -226,30 +336,66 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- epilogue --
-    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const int et = threadIdx.x - 64;  // 0..127
+    const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31
     const int r = quarter * 32 + lane;
     const int n = row0 + r;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(accum, 0));
+    const bool row_ok = r < p.tile_rows && n < p.n;
+    // Scales may come from the previous grid; `out` may still be read by it.
+    pdl_wait();
+    const float *__restrict__ sa = p.sa;
+    for (int m = et; m < p.mpad; m += kEpiThreads) sa_s[m] = m < p.m ? sa[m] : 0.0f;
+    const float wsn = row_ok ? p.ws[n] : 0.0f;
+    epi_barrier();
+    const bool ok = epi_all(mbar_wait(accum, 0));
     tc_fence_after();
-    const bool aborted = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
+    const bool aborted = !epi_all(*abort_flag == 0);
     if (!ok) {
-      if (lane == 0) set_status(p.status, kStatusTimeout);
+      if (et == 0) set_status(p.status, kStatusTimeout);
     } else if (!aborted) {
-      const float wsn = n < p.n ? __ldg(p.ws + n) : 0.0f;
-      for (int c0 = 0; c0 < p.mpad; c0 += 16) {
-        uint32_t v[16];
-        tc_ld16(tmem_d + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
-        if (n < p.n) {
+      int8_t *__restrict__ out = p.out;
+      int32_t *__restrict__ acc_out = p.acc_out;
+      // int8 tile [mpad][tile_rows] for the TMA store, in the stage ring: every
+      // copy into it has landed and every MMA reading it has completed.
+      int8_t *tile = reinterpret_cast<int8_t *>(stages);
+      const bool via_tma = p.tma_store != 0;
+      const uint32_t taddr = tmem_d + ((uint32_t)(quarter * 32) << 16);
+      for (int c0 = 0; c0 < p.mpad; c0 += 32) {
+        const bool two = c0 + 16 < p.mpad;  // uniform across the CTA
+        uint32_t va[16], vb[16];
+        tc_ld16_nowait(taddr + (uint32_t)c0, va);
+        if (two) tc_ld16_nowait(taddr + (uint32_t)(c0 + 16), vb);
+        tc_wait_ld(va, vb);
+        int oa[16], ob[16];
+        requant16(va, sa_s + c0, wsn, p.out_scale, p.inv_out_scale, oa);
+        if (two) requant16(vb, sa_s + c0 + 16, wsn, p.out_scale, p.inv_out_scale, ob);
+        for (int h = 0; h < (two ? 2 : 1); ++h) {
+          const int cb = c0 + 16 * h;
+          const int(&o)[16] = h ? ob : oa;
+          const uint32_t(&v)[16] = h ? vb : va;
+          if (via_tma) {
+            if (r < p.tile_rows) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = c0 + j;
-            if (m < p.m) {
-              const int32_t acc = (int32_t)v[j];
-              p.out[(int64_t)m * p.ldo + n] = requant(acc, __ldg(p.sa + m), wsn, p.out_scale);
-              if (p.acc_out) p.acc_out[(int64_t)m * p.n + n] = acc;
+              for (int j = 0; j < 16; ++j) tile[(cb + j) * p.tile_rows + r] = (int8_t)o[j];
             }
+          } else if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (cb + j < p.m) out[(int64_t)(cb + j) * p.ldo + n] = (int8_t)o[j];
+          }
+          if (acc_out && row_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (cb + j < p.m) acc_out[(int64_t)(cb + j) * p.n + n] = (int32_t)v[j];
           }
         }
+      }
+      if (via_tma) {
+        // generic-proxy writes of the tile -> visible to the bulk-copy engine
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        epi_barrier();
+        // rows >= m and columns >= n fall outside the tensor and are not written
+        if (et == 0) tma_store_2d(&tmap_out, row0, 0, tile);
       }
     }
   }
@@ -318,6 +464,21 @@ bool make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, in
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// int8 matrix [rows, cols] (row stride ld bytes) as a TMA store target, box
+// [box_rows x box_cols], no swizzle; elements outside the tensor are skipped.
+bool make_store_map(CUtensorMap *map, void *base, int64_t rows, int64_t cols, int64_t ld, int box_cols,
+                    int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 bool tc_shape_ok(const GemmI8Launch &a) {
   const auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   return a.m >= 1 && a.m <= kMaxTokens && a.n >= 1 && a.n < (int64_t(1) << 31) && a.k >= 1 &&
@@ -334,6 +495,10 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
   p.sa = a.sa;
   p.ws = a.ws;
   p.out_scale = a.out_scale;
+  {
+    const float inv = 1.0f / a.out_scale;  // IEEE division on the host: RN(1 / out_scale)
+    p.inv_out_scale = std::isfinite(inv) ? inv : 0.0f;
+  }
   p.out = a.out;
   p.ldo = a.ldo;
   p.acc_out = a.acc_out;
@@ -351,19 +516,33 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
   p.mpad = (int32_t)((a.m + 15) / 16 * 16);
   p.nkb = (int32_t)((a.k + kKBlock - 1) / kKBlock);
   p.b_bytes = p.mpad * kKBlock;
-  p.stage_bytes = kTileRows * kKBlock + p.b_bytes;  // multiple of 1024
+  p.stage_bytes = kWTileBytes + p.b_bytes;  // multiple of 1024
   uint32_t cols = 32;
   while (cols < (uint32_t)p.mpad) cols <<= 1;
   p.tmem_cols = cols;
-  const int reserve = 1024 /* alignment slack */ + 1024 /* barriers */;
+  // Rows per CTA: the same share for every SM, at most the MMA's 128.  Every
+  // CTA also reads the whole activation tile (from L2), so a tile is kept at
+  // least half as tall as the padded token count (and at least 16 rows).
+  const int64_t slots = (int64_t)dp.sm_count;
+  const int64_t waves = (a.n + slots * kMmaRows - 1) / (slots * kMmaRows);
+  const int64_t even = (a.n + waves * slots - 1) / (waves * slots);
+  const int64_t floor_rows = std::min<int64_t>(kMmaRows, std::max<int64_t>(16, p.mpad / 2));
+  // multiple of 16 rows: the output tile's TMA store starts at x = row0
+  p.tile_rows = (int32_t)std::min<int64_t>(kMmaRows, (std::max(even, floor_rows) + 15) / 16 * 16);
+  const int grid = (int)((a.n + p.tile_rows - 1) / p.tile_rows);
+  const int reserve = 1024 /* alignment slack */ + kBarRegion + kScaleRegion;
   int nst = (dp.smem_optin - reserve) / p.stage_bytes;
-  nst = std::min(nst, 8);
+  nst = std::min(nst, std::max(1, std::min(kMaxStages, env_int("KS_B200_GEMM_STAGES", 8))));
   nst = std::min(nst, p.nkb);
   if (nst < 1) return cudaErrorInvalidValue;
   p.nst = nst;
-  CUtensorMap mw, ma;
-  if (!make_map(&mw, a.w, a.n, a.k, a.ldw, kTileRows) || !make_map(&ma, a.a, a.m, a.k, a.lda, p.mpad))
+  CUtensorMap mw, ma, mo;
+  if (!make_map(&mw, a.w, a.n, a.k, a.ldw, p.tile_rows) || !make_map(&ma, a.a, a.m, a.k, a.lda, p.mpad))
     return cudaErrorInvalidValue;
+  // int8 output [m, n], row stride ldo: one box [mpad x tile_rows] per CTA.
+  p.tma_store = (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0 && a.ldo % 16 == 0 &&
+                make_store_map(&mo, a.out, a.m, a.n, a.ldo, p.tile_rows, p.mpad);
+  if (!p.tma_store) std::memset(&mo, 0, sizeof(mo));
   const size_t smem = (size_t)reserve + (size_t)nst * p.stage_bytes;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
@@ -372,9 +551,19 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
         cudaFuncSetAttribute(gemm_i8_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dp.smem_optin);
   });
   if (attr_err[device & 63] != cudaSuccess) return attr_err[device & 63];
-  const int grid = (int)((a.n + kTileRows - 1) / kTileRows);
-  gemm_i8_tc_kernel<<<grid, kGemmThreads, smem, stream>>>(mw, ma, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl_enabled(stream)) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel, mw, ma, mo, p);
 }
 
 }  // namespace ksb

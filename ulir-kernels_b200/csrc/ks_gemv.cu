@@ -816,11 +816,6 @@ namespace {
 std::once_flag g_props_once[64];
 DeviceProps g_props[64];
 
-int env_int(const char *name, int dflt) {
-  const char *v = std::getenv(name);
-  return v && *v ? std::atoi(v) : dflt;
-}
-
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int ilog2_exact(int64_t v) {
@@ -865,11 +860,6 @@ bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int
 
 size_t stream_smem_bytes(const StreamGeom &g) {
   return (size_t)kBarBytes + 2 * (size_t)g.xbuf_bytes + (size_t)g.nst * g.stage_bytes;
-}
-
-bool pdl_enabled(cudaStream_t stream) {
-  static const bool on = env_int("KS_B200_PDL", 1) != 0;
-  return on && stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread;
 }
 
 template <class Op, int CW>
@@ -1071,6 +1061,16 @@ bool batch_x_aligned(const GemvBatch &b, int from, int n) {
 }
 
 }  // namespace
+
+int env_int(const char *name, int dflt) {
+  const char *v = std::getenv(name);
+  return v && *v ? std::atoi(v) : dflt;
+}
+
+bool pdl_enabled(cudaStream_t stream) {
+  static const bool on = env_int("KS_B200_PDL", 1) != 0;
+  return on && stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread;
+}
 
 const DeviceProps &device_props(int device) {
   const int d = device & 63;

@@ -68,6 +68,12 @@ struct DeviceProps {
 };
 const DeviceProps &device_props(int device);
 
+// Integer environment knob (tuning only; the default when unset or empty).
+int env_int(const char *name, int dflt);
+// Programmatic dependent launch on this stream: on unless KS_B200_PDL=0, never
+// on the legacy or per-thread default stream.
+bool pdl_enabled(cudaStream_t stream);
+
 cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device);
 cudaError_t launch_i8(const I8Launch &a, cudaStream_t stream, int device);
 
