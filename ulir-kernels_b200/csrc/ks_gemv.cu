@@ -494,49 +494,115 @@ __device__ __forceinline__ uint32_t quant_rne_byte(float v, float s) {
   return (uint32_t)((int)q) & 0xFFu;
 }
 
+// sat_i8(rint(v / s)) without the division, given inv = RN(1/s) finite:
+// q = RN(v * inv) and RN(v / s) both lie within |v/s| * 2^-23 of v/s (3.1e-5
+// while |q| < 129), so rint() can differ between them only across a
+// half-integer.  q is clamped to [-129, 128] (NaN -> -129, as fmaxf does in
+// quant_rne_byte), rounded to an integer by adding 1.5 * 2^23 (ties to even);
+// `near` is set when q lies within 2^-14 of a half-integer, and the caller
+// then takes quant_rne_byte() instead.
+__device__ __forceinline__ uint32_t quant_rne_byte_inv(float v, float inv, bool &near) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float q = fminf(fmaxf(__fmul_rn(v, inv), -129.0f), 128.0f);
+  const float y = __fadd_rn(q, kMagic);
+  near = __fsub_rn(0.5f, fabsf(__fsub_rn(q, __fsub_rn(y, kMagic)))) < 0x1p-14f;
+  const int i = min(max(__float_as_int(y) - 0x4B400000, -128), 127);
+  return (uint32_t)i & 0xFFu;
+}
+
+// Four consecutive f32 (16-byte load when the vector is 16-byte aligned).
+// The chunk loops below are unrolled, so a chunk's loads are independent and
+// cost about one memory latency together, not one each.
+__device__ __forceinline__ float4 load4_f32(const float *p, bool al16) {
+  if (al16) return *reinterpret_cast<const float4 *>(p);
+  return make_float4(p[0], p[1], p[2], p[3]);
+}
+
 // Prepare matrix m's activations into buffer xb.  For f32 inputs every CTA
 // computes the same normalisation / scale from the whole vector, so no extra
 // kernel or global round trip is needed; the quantisation is
 //   s = max|v| / 127 (1 if the vector is all zero),  q = sat_i8(rne(v / s))
 // with v = x, or v = (x * rsqrt-scale) * norm_w for RMSNorm, where
-// rsqrt-scale = 1 / sqrtf(sum(x^2) / K + eps).  Contains consumer barriers:
-// every consumer warp must call it.
+// rsqrt-scale = 1 / sqrtf(sum(x^2) / K + eps).  Each consumer thread owns the
+// chunks c = ctid, ctid + NT, ... in all passes (sum of squares, max, quantise)
+// and sums its chunks in order before the fixed-order CTA reduction, so every
+// CTA computes the same scale.  Contains consumer barriers: every consumer
+// warp must call it.
 template <class Op, int CW>
 __device__ void prep_x_f32(const typename Op::Params &op, const LayerExt &e, uint8_t *xb, float *red, int ctid) {
   constexpr int NT = CW * 32;
+  constexpr int KC = Op::kChunkK;
   const int chunks = op.chunks;
-  const int K = chunks * Op::kChunkK;
+  const int K = chunks * KC;
+  const bool rms = e.xmode == kXRmsNorm;
+  const bool al16 =
+      ((reinterpret_cast<uintptr_t>(e.xf) | (rms ? reinterpret_cast<uintptr_t>(e.norm_w) : 0)) & 15u) == 0;
   float scale = 1.0f;
-  if (e.xmode == kXRmsNorm) {
+  if (rms) {
     float ss = 0.0f;
-    for (int k = ctid; k < K; k += NT) {
-      const float v = e.xf[k];
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    for (int c = ctid; c < chunks; c += NT) {
+#pragma unroll
+      for (int g = 0; g < KC / 4; ++g) {
+        const float4 x = load4_f32(e.xf + (size_t)c * KC + 4 * g, al16);
+        ss = __fadd_rn(ss, __fmul_rn(x.x, x.x));
+        ss = __fadd_rn(ss, __fmul_rn(x.y, x.y));
+        ss = __fadd_rn(ss, __fmul_rn(x.z, x.z));
+        ss = __fadd_rn(ss, __fmul_rn(x.w, x.w));
+      }
     }
     ss = consumers_sum<CW>(ss, red, ctid);
     scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), e.eps)));
   }
-  const bool rms = e.xmode == kXRmsNorm;
-  auto val = [&](int k) -> float {
-    const float v = e.xf[k];
-    return rms ? __fmul_rn(__fmul_rn(v, scale), e.norm_w[k]) : v;
+  // v[k .. k+3], k = c * KC + 4 * g
+  auto vals4 = [&](int c, int g) -> float4 {
+    const size_t k = (size_t)c * KC + 4 * g;
+    float4 v = load4_f32(e.xf + k, al16);
+    if (rms) {
+      const float4 w = load4_f32(e.norm_w + k, al16);
+      v.x = __fmul_rn(__fmul_rn(v.x, scale), w.x);
+      v.y = __fmul_rn(__fmul_rn(v.y, scale), w.y);
+      v.z = __fmul_rn(__fmul_rn(v.z, scale), w.z);
+      v.w = __fmul_rn(__fmul_rn(v.w, scale), w.w);
+    }
+    return v;
   };
   float amax;
   if (e.xmode == kXF32Amax) {
     amax = __uint_as_float(*e.amax_in);
   } else {
     float m = 0.0f;
-    for (int k = ctid; k < K; k += NT) m = fmaxf(m, fabsf(val(k)));
+    for (int c = ctid; c < chunks; c += NT) {
+#pragma unroll
+      for (int g = 0; g < KC / 4; ++g) {
+        const float4 v = vals4(c, g);
+        m = fmaxf(fmaxf(fmaxf(m, fabsf(v.x)), fmaxf(fabsf(v.y), fabsf(v.z))), fabsf(v.w));
+      }
+    }
     amax = consumers_max<CW>(m, red, ctid);
   }
   const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, s);
+  const bool fast = isfinite(inv);
   for (int c = ctid; c < chunks; c += NT) {
+    // all of the chunk's loads first (no branch between them), then the
+    // branch-free quantisation, then at most one branch for near-ties
+    float4 v[Op::kRawWords];
+#pragma unroll
+    for (int w = 0; w < Op::kRawWords; ++w) v[w] = vals4(c, w);
     uint32_t raw[Op::kRawWords];
+    bool any_near = !fast;
 #pragma unroll
     for (int w = 0; w < Op::kRawWords; ++w) {
-      const int k = c * Op::kChunkK + 4 * w;
-      raw[w] = quant_rne_byte(val(k), s) | (quant_rne_byte(val(k + 1), s) << 8) |
-               (quant_rne_byte(val(k + 2), s) << 16) | (quant_rne_byte(val(k + 3), s) << 24);
+      bool n0, n1, n2, n3;
+      raw[w] = quant_rne_byte_inv(v[w].x, inv, n0) | (quant_rne_byte_inv(v[w].y, inv, n1) << 8) |
+               (quant_rne_byte_inv(v[w].z, inv, n2) << 16) | (quant_rne_byte_inv(v[w].w, inv, n3) << 24);
+      any_near = any_near || n0 || n1 || n2 || n3;
+    }
+    if (any_near) {  // rare: a value near a rounding tie (or no usable reciprocal): divide
+#pragma unroll
+      for (int w = 0; w < Op::kRawWords; ++w)
+        raw[w] = quant_rne_byte(v[w].x, s) | (quant_rne_byte(v[w].y, s) << 8) | (quant_rne_byte(v[w].z, s) << 16) |
+                 (quant_rne_byte(v[w].w, s) << 24);
     }
     Op::store_prep(op, raw, c, xb);
     if (e.xq_out && blockIdx.x == 0) {
@@ -661,7 +727,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
   for (int m = 0; m < g.count; ++m) {
     const GemvItem &it = items.it[m];
     const OutRef out{it.y, &items, (int64_t)m * items.mstride + items.row_offset, &ext, m};
-    const uint8_t *xb = xbufs + (size_t)(m & 1) * g.xbuf_bytes;
+    // f32 inputs: one vector (ext.xf) for every matrix of the launch, prepared once
+    const uint8_t *xb = xbufs + (ext.xmode != kXInt8 ? 0 : (size_t)(m & 1) * g.xbuf_bytes);
     uint32_t pre[2][RW];
     const bool more = m + 1 < g.count;
     if (more && prefetch && !stop) {
@@ -699,11 +766,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
       if (lane == 0) mbar_arrive(&empty[b]);
     }
     pair_base += (rows_cta + 1) / 2;
-    if (more) {
+    if (more && ext.xmode == kXInt8) {
       uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
-      if (ext.xmode != kXInt8) {
-        prep_x_f32<Op, CW>(op, ext, xn, red, ctid);  // has barriers: every warp calls it
-      } else if (!stop) {
+      if (!stop) {
         if (ctid == 0) Op::set_sx(op, xn, Op::default_sx(op));
         if (prefetch) {
 #pragma unroll
