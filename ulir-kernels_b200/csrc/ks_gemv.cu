@@ -766,9 +766,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
       if (lane == 0) mbar_arrive(&empty[b]);
     }
     pair_base += (rows_cta + 1) / 2;
-    if (more && ext.xmode == kXInt8) {
+    if (more) {
       uint8_t *xn = xbufs + (size_t)((m + 1) & 1) * g.xbuf_bytes;
-      if (!stop) {
+      // f32 inputs were prepared once for every matrix; the barrier below also
+      // orders this matrix's output stores before the next matrix's epilogue
+      // reads them (silu(gate[r]) * up[r] reads gate rows other warps wrote)
+      if (!stop && ext.xmode == kXInt8) {
         if (ctid == 0) Op::set_sx(op, xn, Op::default_sx(op));
         if (prefetch) {
 #pragma unroll
