@@ -296,6 +296,8 @@ def run_b200_arm(args):
 
     main = torch.cuda.Stream(device=dev)
     comm = torch.cuda.Stream(device=dev)
+    main.wait_stream(torch.cuda.current_stream(dev))  # inputs and zero-filled outputs first
+    comm.wait_stream(torch.cuda.current_stream(dev))
     per_chunk = MATS // CHUNKS
     peer = world > 1 and args.gather == "peer"
     pgw = None
@@ -504,6 +506,9 @@ def run_decode_layers(K, torch, dev, args):
     wp = [(ctypes.c_void_p * 5)(*[t.data_ptr() for t in W]) for W in Ws]
     sp = [(ctypes.c_void_p * 5)(*[t.data_ptr() for t in S]) for S in Ss]
     stream = torch.cuda.Stream(device=dev)
+    # the zero-filled workspace and the inputs are written on the current
+    # stream; the layers run on `stream`
+    stream.wait_stream(torch.cuda.current_stream(dev))
 
     def chain():
         for l in range(n):

@@ -251,13 +251,22 @@ int ks_b200_peer_arrival_wait_async(const uint32_t *counter,
  * quantise(v): s = max|v| / 127 (1 if v is all zero), q = sat_i8(rne(v / s)).
  * weights[5] / scales_f16[5] are qkv, o, gate, up, down: packed int4 (row
  * stride cols/2 bytes) with f16 group scales (row stride cols/group_size).
- * Every step runs inside the four GEMV launches (activation preparation and
- * epilogues are fused; the launches are chained with programmatic dependent
- * launch).  `workspace` (device memory, ks_b200_decode_layer_workspace bytes)
- * receives the intermediates, in this order, each region starting on a
- * 256-byte boundary (ks_b200_decode_layer_offsets gives the 11 offsets and
- * the total): f32 qkv[3h], h2[h], gate[i], up[i], act[i], s1..s4[4],
- * u32 max|act| bits, int8 q1[h], q2[h], q3[h], q4[i].
+ * The whole layer is one cooperative persistent kernel (one CTA per SM: a
+ * producer warp streams all five weight matrices back to back, the consumer
+ * warps run the four stages with a grid barrier between them) when the shape
+ * allows it (hidden <= 8192, inter <= 16384, 16-byte aligned vectors, weights
+ * and scales, scale rows a multiple of 16 bytes); otherwise four GEMV
+ * launches with the same fused preparation and epilogues, chained with
+ * programmatic dependent launch.  KS_B200_DECODE_PERSISTENT=0 forces the
+ * four launches.  `workspace` (device memory, ks_b200_decode_layer_workspace
+ * bytes, zero-filled before its first use, not shared by calls that may run
+ * at the same time) receives the intermediates, in this order, each region
+ * starting on a 256-byte boundary (ks_b200_decode_layer_offsets gives the 11
+ * offsets and the total): f32 qkv[3h], h2[h], gate[i], up[i], act[i],
+ * s1..s4[4], u32 max|act| bits (bytes 128..135 of that 256-byte region hold
+ * the persistent kernel's grid-barrier counter), int8 q1[h], q2[h], q3[h],
+ * q4[i].  After a call whose status reports a timeout, zero the workspace
+ * again before reusing it.
  */
 size_t ks_b200_decode_layer_workspace(size_t hidden, size_t inter);
 int ks_b200_decode_layer_offsets(size_t hidden, size_t inter, size_t *offsets);

@@ -108,6 +108,7 @@ def test_w4a8_batch_graph_capture(ks, cuda):
     dx, dw, ds = _to(torch, cuda, xs), _to(torch, cuda, ws), _to(torch, cuda, ss, view16=True)
     ys = [torch.zeros(rows, dtype=torch.float32, device=cuda) for _ in range(n)]
     stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())  # zero-filled outputs first
     with torch.cuda.stream(stream):
         ks.matvec_w4a8_batch_async(dx, dw, ds, ys, cols // 2, cols // group, rows, cols, group, 0.03, stream=stream)
     stream.synchronize()

@@ -20,8 +20,12 @@ H, I, G, EPS = 4096, 11008, 32, 1e-5
 W4A8_REL_TOL = 1e-4
 
 
-@pytest.fixture(scope="module")
-def layer(cuda, ks):
+@pytest.fixture(scope="module", params=["persistent", "four_launches"])
+def layer(request, cuda, ks):
+    """One layer run twice on one workspace, by the persistent cooperative
+    kernel (the default) or by the four chained launches (its fallback)."""
+    import os
+
     import torch
 
     g = np.random.default_rng(4242)
@@ -44,12 +48,21 @@ def layer(cuda, ks):
     wptr = (ctypes.c_void_p * 5)(*[t.data_ptr() for t in dW])
     sptr = (ctypes.c_void_p * 5)(*[t.data_ptr() for t in dS])
     stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())  # inputs and the zeroed workspace first
 
     def run():
-        ks.check(L.ks_b200_decode_layer_w4a8_async(dh.data_ptr(), out.data_ptr(), dn1.data_ptr(), dn2.data_ptr(),
-                                                   EPS, wptr, sptr, H, I, G, ws.data_ptr(), ws_bytes,
-                                                   status.data_ptr(), ks.stream_handle(stream)))
-        stream.synchronize()
+        old = os.environ.get("KS_B200_DECODE_PERSISTENT")
+        os.environ["KS_B200_DECODE_PERSISTENT"] = "1" if request.param == "persistent" else "0"
+        try:
+            ks.check(L.ks_b200_decode_layer_w4a8_async(dh.data_ptr(), out.data_ptr(), dn1.data_ptr(),
+                                                       dn2.data_ptr(), EPS, wptr, sptr, H, I, G, ws.data_ptr(),
+                                                       ws_bytes, status.data_ptr(), ks.stream_handle(stream)))
+            stream.synchronize()
+        finally:
+            if old is None:
+                del os.environ["KS_B200_DECODE_PERSISTENT"]
+            else:
+                os.environ["KS_B200_DECODE_PERSISTENT"] = old
         return out.cpu().numpy().copy(), ws.cpu().numpy().copy()
 
     y1, w1 = run()
@@ -65,6 +78,10 @@ def layer(cuda, ks):
            "up": region(3, np.float32, I), "act": region(4, np.float32, I), "s": region(5, np.float32, 4),
            "amax": region(6, np.uint32, 1), "q1": region(7, np.int8, H), "q2": region(8, np.int8, H),
            "q3": region(9, np.int8, H), "q4": region(10, np.int8, I), "h_out": y1}
+    # bytes 128..255 of the max|act| region are the persistent kernel's grid
+    # barrier words (a generation counter that advances every call)
+    for w in (w1, w2):
+        w[o[6] + 128:o[6] + 256] = 0
     return dict(W=W, S=S, h=h, n1=n1, n2=n2, gpu=gpu, y2=y2, w2=w2, w1=w1, status=status.cpu().tolist())
 
 

@@ -63,6 +63,7 @@ def _worker(rank, world, port, q):
               for s in ss]
         pg = PeerGatherW4A8(count, rows, dev)
         stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))  # zero-filled buffers first
         with torch.cuda.stream(stream):
             for step in range(3):  # several runs: counters and targets keep growing
                 pg.run(dx, dw, ds, cols, group, 0.02, K.SCALE_F16, stream=stream)

@@ -428,6 +428,7 @@ def test_async_status_and_streams(ks, cuda, oracle):
     status = torch.zeros(ks.STATUS_WORDS, dtype=torch.int32, device=cuda)
     stream = torch.cuda.Stream()
     y = torch.zeros(rows, dtype=torch.float32, device=cuda)
+    stream.wait_stream(torch.cuda.current_stream())  # zero-filled buffers first
     with torch.cuda.stream(stream):
         ks.matvec_w4a8_async(dx, dw, wstride, ds, sstride, y, rows, cols, group, 0.02, status=status, stream=stream)
     stream.synchronize()
@@ -452,6 +453,7 @@ def test_async_graph_capture(ks, cuda, oracle):
     dx, dw, ds = dev(x, cuda), dev(w, cuda), dev(s.view(np.uint16), cuda)
     y = torch.zeros(rows, dtype=torch.float32, device=cuda)
     stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())  # zero-filled output first
     with torch.cuda.stream(stream):  # warm-up outside capture
         ks.matvec_w4a8_async(dx, dw, wstride, ds, sstride, y, rows, cols, group, 0.02, stream=stream)
     stream.synchronize()
