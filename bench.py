@@ -81,11 +81,16 @@ def parse_args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the host-buffer e2e loop")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the INT8 GEMV and skinny GEMM secondary measurements")
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="secondary measurement: a chain of this many fused W4A8 decode layers (0: skip)")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N > 1: output gather by peer stores from the GEMV kernel (default) or NCCL")
     return ap.parse_args()
+
+
+_JSON_OUT = sys.stdout  # replaced in main() by a private copy of the original stdout
 
 
 def dist_env():
@@ -188,7 +193,7 @@ def run_reference_arm(args):
         "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=_JSON_OUT, flush=True)
     return 0
 
 
@@ -426,6 +431,9 @@ def run_b200_arm(args):
     e2e = run_e2e(L, K, torch, dist, dev, world, rank, e2e_steps) if e2e_steps > 0 else None
 
     layer = run_decode_layers(K, torch, dev, args) if args.decode_layers > 0 else None
+    # the other configurations, single GPU only (per-GPU numbers)
+    i8 = run_int8_gemv(K, torch, dev) if world == 1 and not args.no_secondary else None
+    gemm = run_gemm(K, torch, dev) if world == 1 and not args.no_secondary else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -461,12 +469,14 @@ def run_b200_arm(args):
                                     "frac": gemv_bytes() / chain_us / 1e3 / peak,
                                     "note": "64 single-GEMV launches, PDL chain, per GPU"},
             "decode_layer": layer,
+            "int8_gemv": i8,
+            "gemm_i8": gemm,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": CHUNKS * args.steps * world,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=_JSON_OUT, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -543,6 +553,94 @@ def run_decode_layers(K, torch, dev, args):
             "shape": "hidden 4096, inter 11008, W4A8 G32 f16 scales, batch 1, fused RMSNorm/quantise/SiLU/residual"}
 
 
+def _graph_us(torch, stream, fn, units, reps=10):
+    """Device time per unit of `fn` (graph-captured, CUDA events on `stream`)."""
+    with torch.cuda.stream(stream):
+        fn()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+        e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * units)
+    del g
+    return us
+
+
+I8_N, I8_K, I8_SA = 4096, 4096, 0.02
+
+
+def run_int8_gemv(K, torch, dev):
+    """INT8 GEMV with per-channel dequant, y = (f32(acc) * ws) * sa, 4096 x 4096
+    (the reference's CPU-runnable configuration): 64 distinct resident matrices
+    (1.08 GB > L2), as 4 batched launches of 16 and as 64 single launches."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 31)
+    n = 64
+    W = [torch.randint(-127, 128, (I8_N, I8_K), dtype=torch.int8, device=dev, generator=gen) for _ in range(n)]
+    WS = [torch.rand(I8_N, device=dev, generator=gen) * 9e-3 + 1e-3 for _ in range(n)]
+    x = torch.randint(-127, 128, (I8_K,), dtype=torch.int8, device=dev, generator=gen)
+    Y = torch.zeros((n, I8_N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+
+    def batched():
+        for c in range(0, n, 16):
+            K.matvec_i8_batch_async([x] * 16, W[c:c + 16], [Y[j] for j in range(c, c + 16)], I8_K, I8_N, I8_K,
+                                    w_scales=WS[c:c + 16], sa=I8_SA, stream=stream)
+
+    def single():
+        for j in range(n):
+            K.matvec_i8_dequant_async(x, W[j], I8_K, WS[j], I8_SA, Y[j], I8_N, I8_K, stream=stream)
+
+    b = I8_N * I8_K + I8_K + 8 * I8_N  # weights, x, dequant scales, f32 outputs
+    peak, _ = measured_hbm_peak()
+    out = {"shape": f"{I8_N}x{I8_K} int8, per-channel f32 dequant", "bytes_per_gemv": b}
+    for name, fn in (("batched_16", batched), ("single_launch_chain", single)):
+        us = _graph_us(torch, stream, fn, n)
+        out[name] = {"us_per_gemv": us, "GB_s": b / us / 1e3, "frac": b / us / 1e3 / peak}
+    return out
+
+
+def run_gemm(K, torch, dev):
+    """Skinny INT8 GEMM with requantisation, M x 4096 x 14336 (M = 8, 16, 32, 64),
+    output scale 0.05: a graph of 32 launches over 8 distinct weight copies
+    (470 MB > L2) per M."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 47)
+    N, Kd, copies = 14336, 4096, 8
+    W = [torch.randint(-127, 128, (N, Kd), dtype=torch.int8, device=dev, generator=gen) for _ in range(copies)]
+    ws = torch.rand(N, device=dev, generator=gen) * 9e-3 + 1e-3
+    stream = torch.cuda.Stream(device=dev)
+    peak, _ = measured_hbm_peak()
+    out = {"shape": "M x 4096 x 14336 int8 -> int8, per-token / per-channel f32 scales, out scale 0.05",
+           "kernel": "gemm_i8_tc_kernel (tcgen05.mma kind::i8, TMEM accumulators)"}
+    for M in (8, 16, 32, 64):
+        A = torch.randint(-127, 128, (M, Kd), dtype=torch.int8, device=dev, generator=gen)
+        sa = torch.rand(M, device=dev, generator=gen) * 9e-3 + 1e-3
+        o = torch.zeros((M, N), dtype=torch.int8, device=dev)
+        status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+
+        def fn():
+            for i in range(32):
+                K.gemm_i8_requant_async(A, sa, W[i % copies], ws, 0.05, o, M, N, Kd, status=status, stream=stream)
+
+        us = _graph_us(torch, stream, fn, 32, reps=5)
+        assert status.cpu().tolist() == [0, 0]
+        b = N * Kd + M * Kd + M * N + 4 * (M + N)
+        out[f"M{M}"] = {"us": us, "TB_s": b / us / 1e6, "frac": b / us / 1e3 / peak}
+    return out
+
+
 def run_e2e(L, K, torch, dist, dev, world, rank, steps):
     """Host buffers through ks_b200_matvec_w4a8_f16: H2D + kernel + D2H per GEMV."""
     nbuf = 4
@@ -584,7 +682,13 @@ def run_e2e(L, K, torch, dist, dev, world, rank, steps):
 
 
 def main():
+    global _JSON_OUT
     args = parse_args()
+    # The one JSON line is the only thing on stdout: anything libraries write to
+    # file descriptor 1 (NCCL's version banner, for one) goes to stderr.
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference_arm(args)
     return run_b200_arm(args)

@@ -58,7 +58,7 @@ namespace {
 constexpr int kDecCW = 16;  // consumer warps
 constexpr int kDecThreads = (kDecCW + 1) * 32;
 constexpr int kDecMaxSlots = 16;
-constexpr int kDecSlotTarget = 25 * 1024;  // bytes of one ring slot, about
+constexpr int kDecSlotTarget = 64 * 1024;  // bytes of one ring slot, about (fewer, longer copies)
 
 // One stage as both the producer and the consumers walk it.
 struct DecStage {
@@ -73,7 +73,8 @@ struct DecStage {
 struct DecParams {
   DecStage st[4];
   int32_t nslots, slot_bytes, xbuf_bytes;
-  int32_t gshift;  // log2(group / 32)
+  int32_t gshift;    // log2(group / 32)
+  int32_t inflight;  // slots issued and not yet landed, at most (0: up to the ring)
   // activations and workspace
   const float *h_in;
   float *h_out;
@@ -151,7 +152,8 @@ __device__ __forceinline__ uint64_t barrier_base(const unsigned long long *count
 __device__ void grid_barrier(unsigned long long *count, uint64_t base, int k, int ctid, uint32_t *status) {
   consumers_sync<kDecCW>();
   if (ctid == 0) {
-    __threadfence();
+    // release: this CTA's writes (ordered before it by the CTA barrier) are
+    // visible to whoever acquires a count that includes this arrival
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(count) : "memory");
     const uint64_t target = base + (uint64_t)(k + 1) * gridDim.x;
     const uint64_t t0 = globaltimer_ns();
@@ -162,9 +164,8 @@ __device__ void grid_barrier(unsigned long long *count, uint64_t base, int k, in
       }
       __nanosleep(32);
     }
-    __threadfence();
   }
-  consumers_sync<kDecCW>();
+  consumers_sync<kDecCW>();  // the acquire above, passed on to every consumer thread
 }
 
 // ---- input preparation in registers ---------------------------------------
@@ -355,6 +356,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
               stop = true;
               break;
             }
+            // at most `inflight` slots issued and not yet landed: a shorter
+            // memory queue keeps the barrier's and the input loads' latency low
+            if (P.inflight > 0 && gs >= P.inflight) {
+              const int g2 = gs - P.inflight;
+              if (!mbar_wait(&full[g2 % P.nslots], (uint32_t)(g2 / P.nslots) & 1u)) {
+                set_status(P.status, kStatusTimeout);
+                stop = true;
+                break;
+              }
+            }
             const int n = min(S.rps, rows_cta - lo);
             const uint32_t wbytes = (uint32_t)n * (uint32_t)S.row_bytes;
             const uint32_t sbytes = (uint32_t)n * (uint32_t)S.srow_bytes;
@@ -505,7 +516,8 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
         return cudaErrorNotSupported;
     }
     const int rt = S.row_bytes + S.srow_bytes;
-    S.rps = std::max(2, (kDecSlotTarget / rt) & ~1);
+    const int target = std::max(8, env_int("KS_B200_DECODE_SLOT_KB", kDecSlotTarget / 1024)) * 1024;
+    S.rps = std::max(2, (target / rt) & ~1);
     slot = std::max(slot, S.rps * rt);
     xbuf = std::max(xbuf, W4A8Op<__half, 4, false>::xbuf_bytes((int)(cols[s] / 32)));
   }
@@ -522,6 +534,7 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
   int gshift = 0;
   while ((int64_t(32) << gshift) < G) ++gshift;
   P.gshift = gshift;
+  P.inflight = std::max(0, std::min(env_int("KS_B200_DECODE_INFLIGHT", 0), nslots - 1));
   P.h_in = a.h_in;
   P.h_out = a.h_out;
   P.norm1_w = a.norm1_w;
