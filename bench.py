@@ -83,6 +83,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the INT8 GEMV and skinny GEMM secondary measurements")
+    ap.add_argument("--only", choices=["gemm", "int8", "decode"], default=None,
+                    help="run only this secondary measurement on one GPU and print it (small device "
+                         "footprint, for profiling); the headline line is not produced")
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="secondary measurement: a chain of this many fused W4A8 decode layers (0: skip)")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
@@ -283,6 +286,13 @@ def run_b200_arm(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.only:
+        if world > 1:
+            raise SystemExit("--only runs on one GPU")
+        fn = {"gemm": lambda: run_gemm(K, torch, dev), "int8": lambda: run_int8_gemv(K, torch, dev),
+              "decode": lambda: run_decode_layers(K, torch, dev, args)}[args.only]
+        print(json.dumps({"only": args.only, "result": fn()}), file=_JSON_OUT, flush=True)
+        return 0
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     L = K.lib()
