@@ -16,11 +16,13 @@ is missing, `lib()` raises.
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_size_t, c_uint16, c_uint32, c_void_p
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent.parent
-LIB_PATH = PKG_DIR / "lib" / "libkernelsmith.so"
+# the in-tree build; KS_B200_LIBRARY names another build of the same library
+LIB_PATH = Path(os.environ.get("KS_B200_LIBRARY") or (PKG_DIR / "lib" / "libkernelsmith.so"))
 
 KS_OK = 0
 KS_ERR_INVALID_ARG = -1
