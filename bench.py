@@ -83,7 +83,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the INT8 GEMV and skinny GEMM secondary measurements")
-    ap.add_argument("--only", choices=["gemm", "int8", "decode"], default=None,
+    ap.add_argument("--only", choices=["gemm", "int8", "decode", "import"], default=None,
                     help="run only this secondary measurement on one GPU and print it (small device "
                          "footprint, for profiling); the headline line is not produced")
     ap.add_argument("--decode-layers", type=int, default=32,
@@ -290,7 +290,8 @@ def run_b200_arm(args):
         if world > 1:
             raise SystemExit("--only runs on one GPU")
         fn = {"gemm": lambda: run_gemm(K, torch, dev), "int8": lambda: run_int8_gemv(K, torch, dev),
-              "decode": lambda: run_decode_layers(K, torch, dev, args)}[args.only]
+              "decode": lambda: run_decode_layers(K, torch, dev, args),
+              "import": lambda: run_import(K, torch, dev)}[args.only]
         print(json.dumps({"only": args.only, "result": fn()}), file=_JSON_OUT, flush=True)
         return 0
     if world > 1:
@@ -444,6 +445,7 @@ def run_b200_arm(args):
     # the other configurations, single GPU only (per-GPU numbers)
     i8 = run_int8_gemv(K, torch, dev) if world == 1 and not args.no_secondary else None
     gemm = run_gemm(K, torch, dev) if world == 1 and not args.no_secondary else None
+    imp = run_import(K, torch, dev) if world == 1 and not args.no_secondary else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -481,6 +483,7 @@ def run_b200_arm(args):
             "decode_layer": layer,
             "int8_gemv": i8,
             "gemm_i8": gemm,
+            "q4_0_import": imp,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": CHUNKS * args.steps * world,
@@ -649,6 +652,35 @@ def run_gemm(K, torch, dev):
         b = N * Kd + M * Kd + M * N + 4 * (M + N)
         out[f"M{M}"] = {"us": us, "TB_s": b / us / 1e6, "frac": b / us / 1e3 / peak}
     return out
+
+
+def run_import(K, torch, dev):
+    """GGML Q4_0 -> native W4A8 G32 f16 for an 11008 x 4096 matrix (the bench
+    matrix shape), 8 distinct inputs per graph (200 MB read > L2): bytes moved
+    per matrix = Q4_0 blocks read + packed int4 and f16 scales written."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 59)
+    rows, cols, group, n = ROWS, COLS, GROUP, 8
+    src = [torch.randint(0, 256, (rows, cols // 32 * 18), dtype=torch.uint8, device=dev, generator=gen)
+           for _ in range(n)]
+    for t in src:  # finite f16 d in every block
+        t.view(rows, cols // 32, 18)[:, :, 1] = 0x20
+    packed = torch.zeros((n, rows, cols // 2), dtype=torch.uint8, device=dev)
+    scales = torch.zeros((n, rows, cols // group), dtype=torch.float16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+
+    def fn():
+        for i in range(n):
+            K.import_ggml_q4_0_async(src[i], cols // 32 * 18, rows, cols, group, packed[i], cols // 2, scales[i],
+                                     scale_type=K.SCALE_F16, stream=stream)
+
+    us = _graph_us(torch, stream, fn, n)
+    b = rows * (cols // 32) * 18 + rows * cols // 2 + rows * (cols // group) * 2
+    peak, _ = measured_hbm_peak()
+    return {"shape": f"{rows}x{cols} Q4_0 -> W4A8 G{group} f16", "bytes_per_matrix": b, "us_per_matrix": us,
+            "GB_s": b / us / 1e3, "frac": b / us / 1e3 / peak,
+            "kernel": "import_q4_0_kernel (one thread per group, 16-byte packed stores)"}
 
 
 def run_e2e(L, K, torch, dist, dev, world, rank, steps):

@@ -330,6 +330,41 @@ int ks_b200_i8_kernel_path(const void *input, const void *weights,
 int ks_b200_gemm_i8_kernel_path(const void *a, size_t lda, const void *w,
                                 size_t ldw, size_t m, size_t n, size_t k);
 
+/*
+ * Native quantized layout version (no counterpart in the reference's headers;
+ * the reference's design proposes it for its target profiles,
+ * docs/design/DES-015-quantized-layout-abi-and-integration-conversion-paths.md:195-198).
+ * Version 1: W4A8 signed int4, value k in byte k/2 (low nibble for even k),
+ * rows independent, group scales row-major with element k using group
+ * k / group_size; INT8 row-major.  Every kernel and the importer below read or
+ * write this layout; ks_b200_quant_layout_version() returns the value the
+ * library was built with.
+ */
+#define KS_QUANT_LAYOUT_VERSION 1
+int ks_b200_quant_layout_version(void);
+
+/*
+ * GGML Q4_0 weights -> native W4A8, on the GPU (the reference's offline
+ * conversion, DES-015:148-179; no counterpart function in the reference).
+ * blocks: rows x (cols/32) Q4_0 blocks of 18 bytes (f16 d, then 16 bytes:
+ * element j in the low nibble of byte j, element j + 16 in its high nibble,
+ * value (nibble - 8) * d), 2-byte aligned, row stride block_row_stride bytes
+ * (even).  Each native
+ * group of group_size (32..256) is requantised with a positive scale:
+ *   scale = max(max(v) / 7, -min(v) / 8), 1 if that is 0;
+ *   q = clamp(round_half_even(v / scale), -8, 7)
+ * (with KS_B200_SCALE_F16 the scale is rounded to f16 first and the codes are
+ * made with that value).  Output: packed int4 rows (16-byte aligned, stride a
+ * multiple of 16) and scales, ready for ks_matvec_w4a8 / ks_b200_*_w4a8*.
+ * Device pointers, queued on `stream`; not byte-exact to GGML (the reference's
+ * design says so), bit-exact to the same f32 steps on a CPU.
+ */
+int ks_b200_import_ggml_q4_0_async(const void *blocks, size_t block_row_stride,
+                                   size_t rows, size_t cols, size_t group_size,
+                                   uint8_t *packed_weights, size_t packed_stride_bytes,
+                                   void *weight_scales, int scale_type,
+                                   size_t scale_stride, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

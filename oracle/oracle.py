@@ -263,3 +263,65 @@ def decode_layer_stages(orc: Oracle, h, norm1, norm2, eps, W, S16, hidden, inter
     d = gemv(4, out["q4"], out["s4"], hidden, inter)
     out["h_out"] = (out["h2"] + d).astype(np.float32)
     return out
+
+
+# ---- GGML Q4_0 -> native W4A8 (the reference's offline conversion) ----------
+Q4_0_BLOCK_BYTES = 18  # f16 d + 16 bytes of nibbles, 32 elements
+
+
+def q4_0_decode(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """GGML Q4_0 blocks [rows, cols/32 * 18] -> f32 [rows, cols], as the
+    reference's design restates GGML's dequantisation
+    (docs/design/DES-015-quantized-layout-abi-and-integration-conversion-paths.md:155-160):
+    element j < 16 is ((qs[j] & 0x0F) - 8) * d, element j + 16 is ((qs[j] >> 4) - 8) * d."""
+    nb = cols // 32
+    b = np.ascontiguousarray(blocks[:, : nb * Q4_0_BLOCK_BYTES]).reshape(rows, nb, Q4_0_BLOCK_BYTES)
+    d = np.ascontiguousarray(b[:, :, 0:2]).view(np.float16).reshape(rows, nb).astype(np.float32)
+    qs = b[:, :, 2:]
+    lo = (qs & 0x0F).astype(np.int32) - 8
+    hi = (qs >> 4).astype(np.int32) - 8
+    vals = np.concatenate([lo, hi], axis=2).astype(np.float32) * d[:, :, None]
+    return vals.reshape(rows, cols).astype(np.float32)
+
+
+def q4_0_import(blocks: np.ndarray, rows: int, cols: int, group: int, f16_scales: bool):
+    """Q4_0 -> native W4A8 following DES-015:162-174 step by step in f32:
+    per native group scale = max(max(v) / 7, -min(v) / 8), 1 if 0;
+    q = clamp(round_half_even(v / scale), -8, 7); value k in byte k/2, low
+    nibble for even k.  With f16 scales the scale is rounded to f16 first (kept
+    positive and finite) and the codes use that value.  Returns (packed uint8
+    [rows, cols/2], scales f32 or f16-bits uint16 [rows, cols/group])."""
+    v = q4_0_decode(blocks, rows, cols).reshape(rows, cols // group, group)
+    with np.errstate(invalid="ignore"):
+        lo = np.fmin.reduce(v, axis=2)
+        hi = np.fmax.reduce(v, axis=2)
+    scale = np.fmax(hi / np.float32(7), -lo * np.float32(0.125)).astype(np.float32)
+    scale[scale == 0] = np.float32(1)
+    if f16_scales:
+        s16 = scale.astype(np.float16)
+        s16[~(s16 > 0)] = np.uint16(1).view(np.float16)  # smallest positive f16
+        s16[np.isinf(s16)] = np.float16(65504)
+        scale = s16.astype(np.float32)
+    q = np.clip(np.rint(v / scale[:, :, None]), -8, 7).astype(np.int8).reshape(rows, cols)
+    packed = pack_int4(q)
+    return packed, (s16.view(np.uint16) if f16_scales else scale)
+
+
+def q4_0_encode(values: np.ndarray, rng_: np.random.Generator | None = None) -> np.ndarray:
+    """f32 [rows, cols] -> Q4_0 blocks, a test-input generator: GGML's scale
+    convention (d = the block's signed absolute maximum / -8, so d may be
+    negative), nibble = clamp(round(v / d) + 8, 0, 15)."""
+    rows, cols = values.shape
+    nb = cols // 32
+    v = values.reshape(rows, nb, 32).astype(np.float32)
+    idx = np.argmax(np.abs(v), axis=2)
+    mx = np.take_along_axis(v, idx[:, :, None], axis=2)[:, :, 0]
+    d = (mx / np.float32(-8)).astype(np.float16)
+    df = d.astype(np.float32)
+    inv = np.where(df != 0, np.float32(1) / np.where(df != 0, df, np.float32(1)), np.float32(0))
+    q = np.clip(np.round(v * inv[:, :, None]) + 8, 0, 15).astype(np.uint8)
+    qs = (q[:, :, :16] & 0x0F) | ((q[:, :, 16:] & 0x0F) << 4)
+    out = np.zeros((rows, nb, Q4_0_BLOCK_BYTES), np.uint8)
+    out[:, :, 0:2] = d.view(np.uint8).reshape(rows, nb, 2)
+    out[:, :, 2:] = qs
+    return out.reshape(rows, nb * Q4_0_BLOCK_BYTES)

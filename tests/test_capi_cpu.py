@@ -154,3 +154,22 @@ def test_no_cpu_fallback(ks):
     yi = np.zeros(2, np.int32)
     rc = L.ks_matvec_i8(ks.addr(x), ks.addr(x), 32, ks.addr(yi), 2, 32, 0, 0, None, 0)
     assert rc == ks.KS_ERR_DEVICE
+
+
+def test_layout_version_and_importer_argument_checks(ks):
+    """KS_QUANT_LAYOUT_VERSION in the header equals the library's, and the
+    importer rejects bad arguments before touching any device."""
+    import re
+
+    hdr = (ROOT / "include" / "ks_b200.h").read_text()
+    m = re.search(r"#define KS_QUANT_LAYOUT_VERSION (\d+)", hdr)
+    assert m and int(m.group(1)) == ks.lib().ks_b200_quant_layout_version() == 1
+    buf = np.zeros(64, np.uint8)
+    L, E = ks.lib(), ks.KS_ERR_INVALID_ARG
+    a = ks.addr(buf)
+    assert L.ks_b200_import_ggml_q4_0_async(None, 18, 1, 32, 32, a, 32, a, 0, 1, None) == E
+    assert L.ks_b200_import_ggml_q4_0_async(a, 18, 1, 48, 32, a, 32, a, 0, 1, None) == E
+    assert L.ks_b200_import_ggml_q4_0_async(a, 18, 1, 32, 48, a, 32, a, 0, 1, None) == E
+    assert L.ks_b200_import_ggml_q4_0_async(a, 10, 1, 32, 32, a, 32, a, 0, 1, None) == E
+    assert L.ks_b200_import_ggml_q4_0_async(a, 18, 1, 32, 32, a, 8, a, 0, 1, None) == E
+    assert L.ks_b200_import_ggml_q4_0_async(a, 18, 1, 32, 32, a, 32, a, 5, 1, None) == E

@@ -559,6 +559,44 @@ extern "C" int ks_b200_matvec_i8_dequant_async(const int8_t *input, const int8_t
                   weight_zero_point, weight_scales, input_scale, true, stream);
 }
 
+extern "C" int ks_b200_quant_layout_version(void) { return KS_QUANT_LAYOUT_VERSION; }
+
+extern "C" int ks_b200_import_ggml_q4_0_async(const void *blocks, size_t block_row_stride, size_t rows,
+                                              size_t cols, size_t group_size, uint8_t *packed_weights,
+                                              size_t packed_stride_bytes, void *weight_scales, int scale_type,
+                                              size_t scale_stride, void *stream) {
+  if (!blocks || !packed_weights || !weight_scales) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (rows == 0 || cols == 0 || cols % 32)
+    return fail(KS_ERR_INVALID_ARG, "rows must be > 0 and cols a positive multiple of 32 (the Q4_0 block)");
+  if (group_size != 32 && group_size != 64 && group_size != 128 && group_size != 256)
+    return fail(KS_ERR_INVALID_ARG, "group_size must be 32, 64, 128 or 256");
+  if (cols % group_size) return fail(KS_ERR_INVALID_ARG, "cols must be a multiple of group_size");
+  if (scale_type != KS_B200_SCALE_F32 && scale_type != KS_B200_SCALE_F16)
+    return fail(KS_ERR_INVALID_ARG, "scale_type must be KS_B200_SCALE_F32 or KS_B200_SCALE_F16");
+  if (block_row_stride < cols / 32 * 18) return fail(KS_ERR_INVALID_ARG, "block_row_stride < (cols/32) * 18");
+  if ((reinterpret_cast<uintptr_t>(blocks) | block_row_stride) & 1u)
+    return fail(KS_ERR_INVALID_ARG, "Q4_0 blocks must be 2-byte aligned with an even row stride");
+  if (packed_stride_bytes < cols / 2 || packed_stride_bytes % 16 ||
+      (reinterpret_cast<uintptr_t>(packed_weights) & 15u))
+    return fail(KS_ERR_INVALID_ARG, "packed rows must be >= cols/2 bytes, 16-byte aligned with a stride multiple of 16");
+  if (scale_stride < cols / group_size) return fail(KS_ERR_INVALID_ARG, "scale_stride < cols / group_size");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  ImportQ4Launch a{};
+  a.src = static_cast<const uint8_t *>(blocks);
+  a.src_stride = (int64_t)block_row_stride;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group_size;
+  a.packed = packed_weights;
+  a.packed_stride = (int64_t)packed_stride_bytes;
+  a.scales = weight_scales;
+  a.scale_type = scale_type;
+  a.scale_stride = (int64_t)scale_stride;
+  cudaError_t e = launch_import_q4_0(a, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
 extern "C" int ks_b200_w4a8_kernel_path(const void *input, const void *packed_weights,
                                         size_t packed_stride_bytes, const void *weight_scales,
                                         int scale_type, size_t scale_stride, size_t rows,

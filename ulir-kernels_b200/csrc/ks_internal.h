@@ -135,6 +135,19 @@ cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32
                              cudaStream_t stream);
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
 
+// GGML Q4_0 blocks -> native W4A8 (packed int4 + positive group scales).
+struct ImportQ4Launch {
+  const uint8_t *src;     // rows x (cols / 32) blocks of 18 bytes
+  int64_t src_stride;     // bytes between rows of blocks
+  int64_t rows, cols, group;
+  uint8_t *packed;        // [rows][packed_stride], 16-byte aligned rows
+  int64_t packed_stride;
+  void *scales;           // f32 or f16 [rows][scale_stride]
+  int scale_type;         // ScaleType
+  int64_t scale_stride;   // elements
+};
+cudaError_t launch_import_q4_0(const ImportQ4Launch &a, cudaStream_t stream);
+
 // Which kernel family launch_w4a8 / launch_i8 picked for a shape (tests and
 // benchmarks report it): 0 = generic per-element path, 1 = TMA-staged path.
 int w4a8_path(const W4A8Launch &a);

@@ -110,6 +110,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp],
     ),
     "ks_b200_gemm_i8_kernel_path": (c_int, [_vp, _sz, _vp, _sz, _sz, _sz, _sz]),
+    "ks_b200_quant_layout_version": (c_int, []),
+    "ks_b200_import_ggml_q4_0_async": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp, _sz, _vp, c_int, _sz, _vp]),
     "ks_b200_w4a8_kernel_path": (c_int, [_vp, _vp, _sz, _vp, c_int, _sz, _sz, _sz, _sz]),
     "ks_b200_i8_kernel_path": (c_int, [_vp, _vp, _sz, _sz, _sz]),
 }
@@ -204,6 +206,17 @@ def gemm_i8_requant_async(a, sa, w, ws, out_scale, out, m, n, k, lda=None, ldw=N
         lib().ks_b200_gemm_i8_requant_async(
             addr(a), lda or k, addr(sa), addr(w), ldw or k, addr(ws), out_scale, addr(out), ldo or n, m, n, k,
             addr(acc_out), addr(status), stream_handle(stream),
+        )
+    )
+
+
+def import_ggml_q4_0_async(blocks, block_row_stride, rows, cols, group, packed, packed_stride, scales,
+                           scale_type=SCALE_F16, scale_stride=None, stream=None) -> None:
+    """GGML Q4_0 blocks (device) -> packed int4 + positive group scales (device)."""
+    check(
+        lib().ks_b200_import_ggml_q4_0_async(
+            addr(blocks), block_row_stride, rows, cols, group, addr(packed), packed_stride, addr(scales),
+            scale_type, scale_stride or cols // group, stream_handle(stream),
         )
     )
 
