@@ -83,7 +83,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the INT8 GEMV and skinny GEMM secondary measurements")
-    ap.add_argument("--only", choices=["gemm", "int8", "decode", "import"], default=None,
+    ap.add_argument("--only", choices=["gemm", "gemm_w4a8", "int8", "decode", "import"], default=None,
                     help="run only this secondary measurement on one GPU and print it (small device "
                          "footprint, for profiling); the headline line is not produced")
     ap.add_argument("--decode-layers", type=int, default=32,
@@ -291,7 +291,8 @@ def run_b200_arm(args):
             raise SystemExit("--only runs on one GPU")
         fn = {"gemm": lambda: run_gemm(K, torch, dev), "int8": lambda: run_int8_gemv(K, torch, dev),
               "decode": lambda: run_decode_layers(K, torch, dev, args),
-              "import": lambda: run_import(K, torch, dev)}[args.only]
+              "import": lambda: run_import(K, torch, dev),
+              "gemm_w4a8": lambda: run_gemm_w4a8(K, torch, dev)}[args.only]
         print(json.dumps({"only": args.only, "result": fn()}), file=_JSON_OUT, flush=True)
         return 0
     if world > 1:
@@ -446,6 +447,7 @@ def run_b200_arm(args):
     i8 = run_int8_gemv(K, torch, dev) if world == 1 and not args.no_secondary else None
     gemm = run_gemm(K, torch, dev) if world == 1 and not args.no_secondary else None
     imp = run_import(K, torch, dev) if world == 1 and not args.no_secondary else None
+    gw4 = run_gemm_w4a8(K, torch, dev) if world == 1 and not args.no_secondary else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -484,6 +486,7 @@ def run_b200_arm(args):
             "int8_gemv": i8,
             "gemm_i8": gemm,
             "q4_0_import": imp,
+            "gemm_w4a8": gw4,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": CHUNKS * args.steps * world,
@@ -650,6 +653,37 @@ def run_gemm(K, torch, dev):
         us = _graph_us(torch, stream, fn, 32, reps=5)
         assert status.cpu().tolist() == [0, 0]
         b = N * Kd + M * Kd + M * N + 4 * (M + N)
+        out[f"M{M}"] = {"us": us, "TB_s": b / us / 1e6, "frac": b / us / 1e3 / peak}
+    return out
+
+
+def run_gemm_w4a8(K, torch, dev):
+    """Batched W4A8 GEMM on the tensor cores, M x 4096 x 14336 (M = 8, 16, 32,
+    64), G 32, f16 scales: a graph of 32 launches over 8 distinct weight copies
+    (264 MB > L2) per M; bytes = packed weights + scales + activations + f32 out."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + 71)
+    N, Kd, G, copies = 14336, 4096, 32, 8
+    W = [torch.randint(0, 256, (N, Kd // 2), dtype=torch.uint8, device=dev, generator=gen) for _ in range(copies)]
+    S = [(torch.rand((N, Kd // G), device=dev, generator=gen) * 9e-3 + 1e-3).to(torch.float16) for _ in range(copies)]
+    stream = torch.cuda.Stream(device=dev)
+    peak, _ = measured_hbm_peak()
+    out = {"shape": "M x 4096 x 14336 int8 x W4A8 (G 32, f16 scales) -> f32",
+           "kernel": "gemm_w4a8_tc_kernel (int4 unpacked to int8 in shared memory, tcgen05.mma kind::i8)"}
+    for M in (8, 16, 32, 64):
+        A = torch.randint(-127, 128, (M, Kd), dtype=torch.int8, device=dev, generator=gen)
+        sx = torch.rand(M, device=dev, generator=gen) * 0.02 + 0.01
+        y = torch.zeros((M, N), dtype=torch.float32, device=dev)
+        status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+
+        def fn():
+            for i in range(32):
+                K.gemm_w4a8_async(A, sx, W[i % copies], S[i % copies], y, M, N, Kd, G, status=status, stream=stream)
+
+        us = _graph_us(torch, stream, fn, 32, reps=5)
+        assert status.cpu().tolist() == [0, 0]
+        b = N * Kd // 2 + N * (Kd // G) * 2 + M * Kd + 4 * M + 4 * M * N
         out[f"M{M}"] = {"us": us, "TB_s": b / us / 1e6, "frac": b / us / 1e3 / peak}
     return out
 

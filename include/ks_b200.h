@@ -331,6 +331,28 @@ int ks_b200_gemm_i8_kernel_path(const void *a, size_t lda, const void *w,
                                 size_t ldw, size_t m, size_t n, size_t k);
 
 /*
+ * Batched W4A8 GEMM for decode (M = 1..64 tokens; no counterpart in the
+ * reference): for every token m and weight row n
+ *   out[m, n] = a_scales[m] * sum_g f32(acc_g) * scale[n, g],
+ *   acc_g = sum_{k in group g} a[m, k] * w[n, k]      (int32, exact)
+ * a: int8 [m, k] (row stride lda), a_scales: f32 [m]; w: the native packed
+ * int4 rows (ks_matvec_w4a8's layout) with f32 or f16 group scales
+ * (scale_type, row stride scale_stride); zero points 0; out: f32 [m, n]
+ * (row stride ldo).  Each token's row equals ks_matvec_w4a8 for that token up
+ * to the order of the f32 sum.  Runs on the tensor cores (tcgen05.mma
+ * kind::i8 on int4 weights unpacked to int8 in shared memory); needs
+ * m <= 64, k a multiple of 32 and of group_size in {32, 64, 128}, 16-byte
+ * aligned a / weights / scales with lda, packed_stride_bytes and scale-row
+ * bytes multiples of 16, else KS_ERR_UNSUPPORTED.  Device pointers, queued on
+ * `stream`; `status` as for the other asynchronous calls.
+ */
+int ks_b200_gemm_w4a8_async(const int8_t *a, size_t lda, const float *a_scales,
+                            const uint8_t *packed_weights, size_t packed_stride_bytes,
+                            const void *weight_scales, int scale_type, size_t scale_stride,
+                            float *out, size_t ldo, size_t m, size_t n, size_t k,
+                            size_t group_size, uint32_t *status, void *stream);
+
+/*
  * Native quantized layout version (no counterpart in the reference's headers;
  * the reference's design proposes it for its target profiles,
  * docs/design/DES-015-quantized-layout-abi-and-integration-conversion-paths.md:195-198).

@@ -559,6 +559,43 @@ extern "C" int ks_b200_matvec_i8_dequant_async(const int8_t *input, const int8_t
                   weight_zero_point, weight_scales, input_scale, true, stream);
 }
 
+extern "C" int ks_b200_gemm_w4a8_async(const int8_t *a, size_t lda, const float *a_scales,
+                                       const uint8_t *packed_weights, size_t packed_stride_bytes,
+                                       const void *weight_scales, int scale_type, size_t scale_stride, float *out,
+                                       size_t ldo, size_t m, size_t n, size_t k, size_t group_size,
+                                       uint32_t *status, void *stream) {
+  if (!a || !a_scales || !packed_weights || !weight_scales || !out) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (m == 0 || n == 0 || k == 0 || group_size == 0) return fail(KS_ERR_INVALID_ARG, "m, n, k, group_size must be > 0");
+  if (lda < k || ldo < n || packed_stride_bytes < packed_row_bytes(k) || scale_stride < scale_groups(k, group_size))
+    return fail(KS_ERR_INVALID_ARG, "lda >= k, ldo >= n, packed stride >= ceil(k/2), scale stride >= ceil(k/group)");
+  if (scale_type != KS_B200_SCALE_F32 && scale_type != KS_B200_SCALE_F16)
+    return fail(KS_ERR_INVALID_ARG, "scale_type must be KS_B200_SCALE_F32 or KS_B200_SCALE_F16");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  GemmW4A8Launch g{};
+  g.a = a;
+  g.lda = (int64_t)lda;
+  g.sx = a_scales;
+  g.w = packed_weights;
+  g.wstride = (int64_t)packed_stride_bytes;
+  g.s = weight_scales;
+  g.sstride = (int64_t)scale_stride;
+  g.stype = scale_type;
+  g.y = out;
+  g.ldy = (int64_t)ldo;
+  g.m = (int64_t)m;
+  g.n = (int64_t)n;
+  g.k = (int64_t)k;
+  g.group = (int64_t)group_size;
+  g.status = status;
+  if (!gemm_w4a8_supported(g))
+    return fail(KS_ERR_UNSUPPORTED,
+                "tensor-core W4A8 GEMM needs m <= 64, k a multiple of 32 and of group_size (32, 64 or 128), "
+                "16-byte aligned a / weights / scales with lda, packed stride and scale-row bytes multiples of 16");
+  cudaError_t e = launch_gemm_w4a8(g, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
 extern "C" int ks_b200_quant_layout_version(void) { return KS_QUANT_LAYOUT_VERSION; }
 
 extern "C" int ks_b200_import_ggml_q4_0_async(const void *blocks, size_t block_row_stride, size_t rows,

@@ -135,6 +135,24 @@ cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32
                              cudaStream_t stream);
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
 
+// Batched W4A8 GEMM (tokens x native int4 weights, group scales) on tcgen05.
+struct GemmW4A8Launch {
+  const int8_t *a;      // [m, k] int8, row stride lda
+  int64_t lda;
+  const float *sx;      // [m] per-token activation scales
+  const uint8_t *w;     // [n, k/2] packed int4, row stride wstride bytes
+  int64_t wstride;
+  const void *s;        // [n, k/group] f32 or f16, row stride sstride elements
+  int64_t sstride;
+  int stype;            // ScaleType
+  float *y;             // [m, n], row stride ldy
+  int64_t ldy;
+  int64_t m, n, k, group;
+  uint32_t *status;
+};
+bool gemm_w4a8_supported(const GemmW4A8Launch &a);
+cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int device);
+
 // GGML Q4_0 blocks -> native W4A8 (packed int4 + positive group scales).
 struct ImportQ4Launch {
   const uint8_t *src;     // rows x (cols / 32) blocks of 18 bytes

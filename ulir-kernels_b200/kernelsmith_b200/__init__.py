@@ -111,6 +111,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ks_b200_gemm_i8_kernel_path": (c_int, [_vp, _sz, _vp, _sz, _sz, _sz, _sz]),
     "ks_b200_quant_layout_version": (c_int, []),
+    "ks_b200_gemm_w4a8_async": (
+        c_int,
+        [_vp, _sz, _vp, _vp, _sz, _vp, c_int, _sz, _vp, _sz, _sz, _sz, _sz, _sz, _vp, _vp],
+    ),
     "ks_b200_import_ggml_q4_0_async": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp, _sz, _vp, c_int, _sz, _vp]),
     "ks_b200_w4a8_kernel_path": (c_int, [_vp, _vp, _sz, _vp, c_int, _sz, _sz, _sz, _sz]),
     "ks_b200_i8_kernel_path": (c_int, [_vp, _vp, _sz, _sz, _sz]),
@@ -206,6 +210,17 @@ def gemm_i8_requant_async(a, sa, w, ws, out_scale, out, m, n, k, lda=None, ldw=N
         lib().ks_b200_gemm_i8_requant_async(
             addr(a), lda or k, addr(sa), addr(w), ldw or k, addr(ws), out_scale, addr(out), ldo or n, m, n, k,
             addr(acc_out), addr(status), stream_handle(stream),
+        )
+    )
+
+
+def gemm_w4a8_async(a, sx, w, s, out, m, n, k, group, lda=None, w_stride=None, s_stride=None, ldo=None,
+                    scale_type=SCALE_F16, status=None, stream=None) -> None:
+    """Batched W4A8 GEMM: out[m, n] = sx[m] * sum_g acc_g * s[n, g] (device buffers)."""
+    check(
+        lib().ks_b200_gemm_w4a8_async(
+            addr(a), lda or k, addr(sx), addr(w), w_stride or (k + 1) // 2, addr(s), scale_type,
+            s_stride or -(-k // group), addr(out), ldo or n, m, n, k, group, addr(status), stream_handle(stream),
         )
     )
 
