@@ -58,7 +58,6 @@ METRIC = "INT8/W4A8 GEMV weight-stream TB/s & % HBM peak at 1/2/4/8 B200"
 ROWS, COLS, GROUP = 11008, 4096, 32
 SX = 0.02
 MATS = 64
-CHUNKS = 4
 SEED = 20261201
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
@@ -88,6 +87,8 @@ def parse_args():
                          "footprint, for profiling); the headline line is not produced")
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="secondary measurement: a chain of this many fused W4A8 decode layers (0: skip)")
+    ap.add_argument("--gemvs-per-launch", type=int, default=0,
+                    help="GEMVs per batched launch (default 64; 16 with --gather nccl)")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="N > 1: output gather by peer stores from the GEMV kernel (default) or NCCL")
     return ap.parse_args()
@@ -298,6 +299,12 @@ def run_b200_arm(args):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     L = K.lib()
+    # launches per step: one batched launch of all 64 GEMVs, except with the
+    # NCCL gather, whose all-gathers overlap the next launch of 16
+    per_launch = args.gemvs_per_launch or (16 if world > 1 and args.gather == "nccl" else MATS)
+    if MATS % per_launch:
+        raise SystemExit(f"--gemvs-per-launch must divide {MATS}")
+    CHUNKS = MATS // per_launch
 
     # ---- resident inputs: 64 shards of [ROWS, COLS] (this rank's rows) ----
     gen = torch.Generator(device=dev)
@@ -325,7 +332,7 @@ def run_b200_arm(args):
     signals = [0] * CHUNKS
 
     def gemv_chunk(c):
-        # one batched launch: 16 independent GEMVs streamed back to back
+        # one batched launch: per_chunk independent GEMVs streamed back to back
         ms = range(c * per_chunk, (c + 1) * per_chunk)
         if peer:
             signals[c] = pgw.run([X[m] for m in ms], [W[m] for m in ms], [S[m] for m in ms], COLS, GROUP, SX,
@@ -341,7 +348,7 @@ def run_b200_arm(args):
             K.matvec_w4a8_async(X[m], W[m], COLS // 2, S[m], COLS // GROUP, Yloc[m // per_chunk, m % per_chunk],
                                 ROWS, COLS, GROUP, SX, scale_type=K.SCALE_F16, status=status, stream=main)
 
-    # one CUDA graph per chunk of 16 GEMVs (launch-bound inner loop)
+    # one CUDA graph per batched launch
     graphs = []
     with torch.cuda.stream(main):
         for c in range(CHUNKS):
@@ -476,7 +483,7 @@ def run_b200_arm(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_GEMV, "traffic_per": "GEMV (ncu capture)",
-                         "kernel": "gemv_stream_kernel<W4A8Op<__half,4,false>,16> (batched, 16 GEMVs per launch)",
+                         "kernel": f"gemv_stream_kernel<W4A8Op<__half,4,false>,16> (batched, {MATS // CHUNKS} GEMVs per launch)",
                          "bytes_per_gemv": gemv_bytes(), "us_per_gemv": per_launch_s * 1e6,
                          "gemvs_per_launch": MATS // CHUNKS},
             "single_launch_chain": {"us_per_gemv": chain_us, "GB_s": gemv_bytes() / chain_us / 1e3,

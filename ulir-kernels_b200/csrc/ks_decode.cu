@@ -173,8 +173,8 @@ __device__ void grid_barrier(unsigned long long *count, uint64_t base, int k, in
 // stage's input vector, i.e. words 2q, 2q+1 (q = group % 4) of chunk group / 4,
 // and keeps them in registers from the load through the quantisation: one
 // memory round trip per stage.  The prepared layout is W4A8Op::store_prep's:
-// even-k bytes of the chunk's word pairs at xb + 32c + 4q, odd-k bytes at
-// xb + 32c + 16 + 4q, kc = 8 * sum(chunk) at xb + 32 * chunks + 4c (zero
+// even-k bytes of the chunk's word pairs at xb + 16c + 4q, odd-k bytes at
+// xb + 16 * chunks + 16c + 4q, kc = 8 * sum(chunk) at xb + 32 * chunks + 4c (zero
 // points are 0), the scale at xb + 36 * chunks.
 constexpr int kNT = kDecCW * 32;
 
@@ -253,8 +253,8 @@ __device__ void prep_groups(int K, int mode, float (&v)[J][8], const float (&nw)
                  (quant_rne_byte(v[j][4 * h + 2], s) << 16) | (quant_rne_byte(v[j][4 * h + 3], s) << 24);
       }
       const int c = gi >> 2, q = gi & 3;
-      *reinterpret_cast<uint32_t *>(xb + 32 * c + 4 * q) = prmt(w[0], w[1], 0x6420);
-      *reinterpret_cast<uint32_t *>(xb + 32 * c + 16 + 4 * q) = prmt(w[0], w[1], 0x7531);
+      *reinterpret_cast<uint32_t *>(xb + 16 * c + 4 * q) = prmt(w[0], w[1], 0x6420);
+      *reinterpret_cast<uint32_t *>(xb + 16 * chunks + 16 * c + 4 * q) = prmt(w[0], w[1], 0x7531);
       if (xq_out && blockIdx.x == 0) *reinterpret_cast<uint2 *>(xq_out + 8 * (size_t)gi) = make_uint2(w[0], w[1]);
     }
     int sum = dp4a_ss(w[1], 0x01010101u, dp4a_ss(w[0], 0x01010101u, 0));

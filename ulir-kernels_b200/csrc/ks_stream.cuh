@@ -250,9 +250,11 @@ __device__ __forceinline__ int w4a8_chunk_dot(const uint4 v, const uint4 xe, con
   return acc;
 }
 
-// Prepared activations, per 32-element chunk c: at xb + 32c the even-k bytes
-// of the chunk's four packed words, at xb + 32c + 16 the odd-k bytes, and at
-// xb + 32*chunks + 4c the constant kc = (8 + zw) * sum(x - zx).
+// Prepared activations, per 32-element chunk c: at xb + 16c the even-k bytes
+// of the chunk's four packed words, at xb + 16*chunks + 16c the odd-k bytes,
+// and at xb + 32*chunks + 4c the constant kc = (8 + zw) * sum(x - zx).  Lanes
+// read consecutive chunks, so both byte planes are read without bank
+// conflicts (16 contiguous bytes per lane).
 // ZX: input zero point != 0.
 template <typename ST, int NCPL, bool ZX>
 struct W4A8Op {
@@ -286,9 +288,8 @@ struct W4A8Op {
       sumx = dp4a_ss(X[2 * q], 0x01010101u, sumx);
       sumx = dp4a_ss(X[2 * q + 1], 0x01010101u, sumx);
     }
-    uint4 *d = reinterpret_cast<uint4 *>(xb + 32 * c);
-    d[0] = make_uint4(e[0], e[1], e[2], e[3]);
-    d[1] = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4 *>(xb + 16 * c) = make_uint4(e[0], e[1], e[2], e[3]);
+    *reinterpret_cast<uint4 *>(xb + 16 * p.chunks + 16 * c) = make_uint4(o[0], o[1], o[2], o[3]);
     reinterpret_cast<int *>(xb + 32 * p.chunks)[c] = (8 + p.zw) * (sumx - 32 * p.zx);
   }
 
@@ -315,8 +316,8 @@ struct W4A8Op {
     for (int j = 0; j < NCPL; ++j) {
       const int c = lane + 32 * j;
       if (c < p.chunks) {
-        const uint4 xe = lds128(xb + 32 * c);
-        const uint4 xo = lds128(xb + 32 * c + 16);
+        const uint4 xe = lds128(xb + 16 * c);
+        const uint4 xo = lds128(xb + 16 * p.chunks + 16 * c);
         const int kc = (int)lds_u32(xb + 32 * p.chunks + 4 * c);
         const int g = c >> p.gshift;
         const uint4 va = lds128(wa + 16 * c);
