@@ -75,6 +75,7 @@ struct DecParams {
   int32_t nslots, slot_bytes, xbuf_bytes;
   int32_t gshift;    // log2(group / 32)
   int32_t inflight;  // slots issued and not yet landed, at most (0: up to the ring)
+  int32_t l2_ahead;  // slots prefetched into L2 ahead of their copy
   // activations and workspace
   const float *h_in;
   float *h_out;
@@ -341,6 +342,35 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
+      // L2 prefetch cursor, l2_ahead slots ahead of the copies: while the
+      // consumers sit at a grid barrier and the ring is full, HBM keeps
+      // streaming the next slots into L2, and their copies then come from L2.
+      int cs = 0, cm = 0, clo = 0, cn = 0;
+      int64_t cr0 = 0;
+      rows_of(P.st[0], cr0, cn);
+      auto settle = [&]() {
+        while (cs < 4 && clo >= cn) {
+          clo = 0;
+          if (++cm >= P.st[cs].count) {
+            cm = 0;
+            if (++cs < 4) rows_of(P.st[cs], cr0, cn);
+          }
+        }
+      };
+      auto advance = [&]() {
+        clo += P.st[cs].rps;
+        settle();
+      };
+      auto prefetch = [&]() {
+        const DecStage &S = P.st[cs];
+        const uint32_t n = (uint32_t)min(S.rps, cn - clo);
+        bulk_prefetch_l2(S.w[cm] + (cr0 + clo) * S.row_bytes, n * (uint32_t)S.row_bytes);
+        bulk_prefetch_l2(S.s[cm] + (cr0 + clo) * S.srow_bytes, n * (uint32_t)S.srow_bytes);
+        advance();
+      };
+      settle();
+      for (int j = 0; j < P.nslots && cs < 4; ++j) advance();
+      for (int j = 0; j < P.l2_ahead && cs < 4; ++j) prefetch();
       int gs = 0;
       bool stop = false;
       for (int s = 0; s < 4 && !stop; ++s) {
@@ -373,6 +403,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
             mbar_arrive_expect_tx(&full[b], wbytes + sbytes);
             bulk_g2s_hint(dst, S.w[m] + (r0 + lo) * S.row_bytes, wbytes, &full[b], pol);
             bulk_g2s(dst + (size_t)S.rps * S.row_bytes, S.s[m] + (r0 + lo) * S.srow_bytes, sbytes, &full[b]);
+            if (gs >= P.nslots && P.l2_ahead > 0 && cs < 4) prefetch();
           }
         }
       }
@@ -535,6 +566,9 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
   while ((int64_t(32) << gshift) < G) ++gshift;
   P.gshift = gshift;
   P.inflight = std::max(0, std::min(env_int("KS_B200_DECODE_INFLIGHT", 0), nslots - 1));
+  // off by default: measured slower (the prefetches queue ahead of the
+  // grid barrier's and the input vector's latency-bound accesses)
+  P.l2_ahead = std::max(0, env_int("KS_B200_DECODE_L2_AHEAD", 0));
   P.h_in = a.h_in;
   P.h_out = a.h_out;
   P.norm1_w = a.norm1_w;

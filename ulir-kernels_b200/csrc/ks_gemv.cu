@@ -85,6 +85,31 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
     // Weights and scales do not depend on the previous kernel: no wait here.
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
+      // Stages beyond the ring are prefetched into L2 l2_ahead stages before
+      // their copy: HBM keeps streaming while the ring is full (consumers
+      // waiting for the previous kernel or for the activations), and the
+      // copies of those stages then come from L2.
+      auto prefetch_stage = [&](int j) {
+        const GemvItem &it = items.it[j / nstages];
+        const int lo = (j % nstages) * g.rps;
+        const int n = min(g.rps, rows_cta - lo);
+        const uint8_t *wsrc = it.w + (r0 + lo) * g.wstride;
+        if (g.w_contig) {
+          bulk_prefetch_l2(wsrc, (uint32_t)n * (uint32_t)g.row_bytes);
+        } else {
+          for (int r = 0; r < n; ++r) bulk_prefetch_l2(wsrc + (int64_t)r * g.wstride, (uint32_t)g.row_bytes);
+        }
+        if (g.srow_bytes) {
+          const uint8_t *ssrc = it.s + (r0 + lo) * g.sstride;
+          if (g.s_contig) {
+            bulk_prefetch_l2(ssrc, (uint32_t)n * (uint32_t)g.srow_bytes);
+          } else {
+            for (int r = 0; r < n; ++r) bulk_prefetch_l2(ssrc + (int64_t)r * g.sstride, (uint32_t)g.srow_bytes);
+          }
+        }
+      };
+      const int ahead = g.l2_ahead;
+      for (int j = g.nst; j < min(total, g.nst + ahead); ++j) prefetch_stage(j);
       int gs = 0;
       bool stop = false;
       for (int m = 0; m < g.count && !stop; ++m) {
@@ -122,6 +147,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
                          &full[b]);
             }
           }
+          if (ahead > 0 && gs >= g.nst && gs + ahead < total) prefetch_stage(gs + ahead);
         }
       }
       if (total <= g.nst) pdl_launch_dependents();
@@ -331,9 +357,14 @@ int ilog2_exact(int64_t v) {
 
 // Fill the ring geometry for one configuration (single or batch); false if
 // the rows are too long to stage.
+// l2_ahead: L2 prefetch distance in stages (measured best on B200: W4A8 1
+// single / 2 batched, INT8 1 single / 0 batched; farther prefetches compete
+// with the ring's own copies).
 bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int xbuf_bytes, int sm_count,
-                 bool batch, int cw) {
+                 bool batch, int cw, int l2_ahead) {
   static const int min_single = std::max(2, env_int("KS_B200_MIN_STAGES", 2));
+  static const int ahead_single = env_int("KS_B200_L2_AHEAD_SINGLE", -1);
+  static const int ahead_batch = env_int("KS_B200_L2_AHEAD_BATCH", -1);
   static const int rps_cap_batch = std::max(2, env_int("KS_B200_BATCH_ROWS_PER_STAGE", 24));
   const int smem_cta = batch ? kSmemBatch : kSmemSingle;
   const int min_stages = batch ? 4 : min_single;
@@ -359,6 +390,8 @@ bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int
   g.srow_bytes = srow_bytes;
   g.stage_bytes = stage_bytes;
   g.xbuf_bytes = xbuf_bytes;
+  const int ahead_env = batch ? ahead_batch : ahead_single;
+  g.l2_ahead = ahead_env >= 0 ? ahead_env : l2_ahead;
   return true;
 }
 
@@ -421,7 +454,7 @@ W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch) {
   const int xbuf = ((chunks * 36 + 4 + 127) / 128) * 128;
   StreamGeom g{};
   if (!plan_stream(g, a.rows, (int)(a.cols / 2), (int)(groups * ssize), xbuf, device_props(device).sm_count,
-                   batch, batch ? 16 : 8))
+                   batch, batch ? 16 : 8, batch ? 2 : 1))
     return P;
   g.wstride = a.wstride;
   g.sstride = a.sstride * ssize;
@@ -481,7 +514,8 @@ I8Plan plan_i8(const I8Launch &a, int device, bool batch) {
   const int chunks = (int)(a.cols / 16);
   const int xbuf = ((chunks * 20 + 127) / 128) * 128;
   StreamGeom g{};
-  if (!plan_stream(g, a.rows, (int)a.cols, 0, xbuf, device_props(device).sm_count, batch, batch ? 16 : 8))
+  if (!plan_stream(g, a.rows, (int)a.cols, 0, xbuf, device_props(device).sm_count, batch, batch ? 16 : 8,
+                   batch ? 0 : 1))
     return P;
   g.wstride = a.wstride;
   g.sstride = 0;

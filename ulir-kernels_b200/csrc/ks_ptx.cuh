@@ -90,6 +90,12 @@ __device__ __forceinline__ void bulk_g2s_hint(void *dst_smem, const void *src_gm
       : "memory");
 }
 
+// Start loading [src, src + bytes) into L2 (bulk prefetch: a hint with no
+// completion to wait for).  src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src_gmem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src_gmem), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

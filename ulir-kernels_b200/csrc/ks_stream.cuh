@@ -132,6 +132,7 @@ struct StreamGeom {
   int32_t w_contig;     // wstride == row_bytes: one copy per stage
   int32_t s_contig;
   int32_t x_al16;       // every activation vector 16-byte aligned
+  int32_t l2_ahead;     // stages prefetched into L2 ahead of the ring
   uint32_t *status;
 };
 
