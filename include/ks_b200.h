@@ -353,6 +353,36 @@ int ks_b200_gemm_w4a8_async(const int8_t *a, size_t lda, const float *a_scales,
                             size_t group_size, uint32_t *status, void *stream);
 
 /*
+ * W4A8 GEMV on f32 activations (no counterpart in the reference): the input
+ * is quantised per token on the device, s = max|input| / 127 (1 if all zero),
+ * q = sat_i8(round_half_even(input / s)), then
+ *   output[r] = s * sum_g f32(acc_g) * scale[r, g]
+ * exactly as ks_matvec_w4a8 / ks_b200_matvec_w4a8_async with that q and
+ * input_scale = s (zero points 0).  quantized_input (int8 [cols]) and
+ * input_scale (one float) receive q and s when not NULL.  Streaming kernel
+ * only: cols a multiple of 32, group_size a power-of-two multiple of 32,
+ * scale-row bytes a multiple of 16, 16-byte aligned input / weights / scales
+ * with strides multiples of 16, else KS_ERR_UNSUPPORTED.  Device pointers,
+ * queued on `stream`; `status` as for the other asynchronous calls.
+ */
+int ks_b200_matvec_w4a8_f32in_async(const float *input, const uint8_t *packed_weights,
+                                    size_t packed_stride_bytes, const void *weight_scales,
+                                    int scale_type, size_t scale_stride, float *output,
+                                    size_t rows, size_t cols, size_t group_size,
+                                    int8_t *quantized_input, float *input_scale,
+                                    uint32_t *status, void *stream);
+
+/*
+ * Per-token activation quantisation (the rule above) of n_tokens rows of f32
+ * x (row stride ldx elements) into int8 q (row stride ldq) and f32 scales
+ * [n_tokens]: the a / a_scales operands of ks_b200_gemm_w4a8_async.  Device
+ * pointers, queued on `stream`.
+ */
+int ks_b200_quantize_per_token_async(const float *x, size_t ldx, size_t n_tokens,
+                                     size_t cols, int8_t *q, size_t ldq, float *scales,
+                                     void *stream);
+
+/*
  * Native quantized layout version (no counterpart in the reference's headers;
  * the reference's design proposes it for its target profiles,
  * docs/design/DES-015-quantized-layout-abi-and-integration-conversion-paths.md:195-198).

@@ -596,6 +596,54 @@ extern "C" int ks_b200_gemm_w4a8_async(const int8_t *a, size_t lda, const float 
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
 }
 
+extern "C" int ks_b200_matvec_w4a8_f32in_async(const float *input, const uint8_t *packed_weights,
+                                               size_t packed_stride_bytes, const void *weight_scales, int scale_type,
+                                               size_t scale_stride, float *output, size_t rows, size_t cols,
+                                               size_t group_size, int8_t *quantized_input, float *input_scale,
+                                               uint32_t *status, void *stream) {
+  if (!input || !packed_weights || !weight_scales || !output) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (rows == 0 || cols == 0 || group_size == 0) return fail(KS_ERR_INVALID_ARG, "rows, cols, group_size must be > 0");
+  if (packed_stride_bytes < packed_row_bytes(cols) || scale_stride < scale_groups(cols, group_size))
+    return fail(KS_ERR_INVALID_ARG, "packed stride >= ceil(cols/2), scale stride >= ceil(cols/group)");
+  if (scale_type != KS_B200_SCALE_F32 && scale_type != KS_B200_SCALE_F16)
+    return fail(KS_ERR_INVALID_ARG, "scale_type must be KS_B200_SCALE_F32 or KS_B200_SCALE_F16");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  W4A8Launch a{};
+  a.w = packed_weights;
+  a.wstride = (int64_t)packed_stride_bytes;
+  a.s = weight_scales;
+  a.sstride = (int64_t)scale_stride;
+  a.stype = scale_type;
+  a.y = output;
+  a.rows = (int64_t)rows;
+  a.cols = (int64_t)cols;
+  a.group = (int64_t)group_size;
+  a.sx = 1.0f;
+  a.status = status;
+  cudaError_t e = launch_w4a8_f32in(a, input, quantized_input, input_scale, static_cast<cudaStream_t>(stream), dev);
+  if (e == cudaErrorNotSupported) {
+    cudaGetLastError();
+    return fail(KS_ERR_UNSUPPORTED,
+                "f32-input W4A8 GEMV needs the streaming kernel's shape: cols a multiple of 32, group a power-of-two "
+                "multiple of 32, scale-row bytes a multiple of 16, 16-byte aligned input, weights and scales");
+  }
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_quantize_per_token_async(const float *x, size_t ldx, size_t n_tokens, size_t cols,
+                                                int8_t *q, size_t ldq, float *scales, void *stream) {
+  if (!x || !q || !scales) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (n_tokens == 0 || cols == 0) return fail(KS_ERR_INVALID_ARG, "n_tokens and cols must be > 0");
+  if (ldx < cols || ldq < cols) return fail(KS_ERR_INVALID_ARG, "ldx >= cols and ldq >= cols");
+  if (n_tokens > 0x7FFFFFFF) return fail(KS_ERR_INVALID_ARG, "n_tokens too large");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  cudaError_t e = launch_quantize_tokens(x, (int64_t)ldx, (int64_t)n_tokens, (int64_t)cols, q, (int64_t)ldq, scales,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
 extern "C" int ks_b200_quant_layout_version(void) { return KS_QUANT_LAYOUT_VERSION; }
 
 extern "C" int ks_b200_import_ggml_q4_0_async(const void *blocks, size_t block_row_stride, size_t rows,

@@ -646,6 +646,27 @@ cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device) {
   return launch_w4a8_cw<8>(P, a.stype, items, stream, device);
 }
 
+// f32 activations, quantised per token inside the kernel (s = max|x| / 127,
+// round half to even; the decode layer's kXF32 preparation), then the W4A8
+// GEMV.  Streaming kernel only (its shape rules, 16-byte aligned x, zero
+// points 0), else cudaErrorNotSupported.
+cudaError_t launch_w4a8_f32in(const W4A8Launch &a, const float *xf, int8_t *xq_out, float *xs_out,
+                              cudaStream_t stream, int device) {
+  if (!aligned16(a.w) || !aligned16(a.s) || !aligned16(xf) || a.zx != 0 || a.zw != 0) return cudaErrorNotSupported;
+  W4A8Plan P = plan_w4a8(a, device, false);
+  if (!P.fast) return cudaErrorNotSupported;
+  LayerExt ext{};
+  ext.xmode = kXF32;
+  ext.xf = xf;
+  ext.xq_out = xq_out;
+  ext.xs_out = xs_out;
+  GemvItems items{};
+  items.it[0] = GemvItem{nullptr, a.w, reinterpret_cast<const uint8_t *>(a.s), a.y};
+  P.g.count = 1;
+  P.g.x_al16 = 1;
+  return launch_w4a8_cw<8>(P, a.stype, items, stream, device, ext);
+}
+
 cudaError_t launch_w4a8_batch(const W4A8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device) {
   if (b.count <= 0) return cudaSuccess;
   W4A8Plan P;

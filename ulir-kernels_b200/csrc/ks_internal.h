@@ -90,6 +90,13 @@ struct GemvBatch {
   void *const *y;
 };
 cudaError_t launch_w4a8_batch(const W4A8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device);
+// f32 activations quantised per token in the kernel; a.x is unused.
+cudaError_t launch_w4a8_f32in(const W4A8Launch &a, const float *xf, int8_t *xq_out, float *xs_out,
+                              cudaStream_t stream, int device);
+// Per-token int8 quantisation of n rows of f32 (s = max|x| / 127, 1 if 0;
+// q = sat_i8(rne(x / s))).
+cudaError_t launch_quantize_tokens(const float *x, int64_t ldx, int64_t n, int64_t cols, int8_t *q, int64_t ldq,
+                                   float *scales, cudaStream_t stream);
 cudaError_t launch_i8_batch(const I8Launch &shape, const GemvBatch &b, cudaStream_t stream, int device);
 
 // Sharded W4A8 batch whose outputs are gathered by peer stores (see the

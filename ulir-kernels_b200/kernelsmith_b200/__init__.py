@@ -118,6 +118,18 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ks_b200_import_ggml_q4_0_async": (c_int, [_vp, _sz, _sz, _sz, _sz, _vp, _sz, _vp, c_int, _sz, _vp]),
     "ks_b200_w4a8_kernel_path": (c_int, [_vp, _vp, _sz, _vp, c_int, _sz, _sz, _sz, _sz]),
     "ks_b200_i8_kernel_path": (c_int, [_vp, _vp, _sz, _sz, _sz]),
+    "ks_b200_matvec_w4a8_f32in_async": (
+        c_int,
+        [_vp, _vp, _sz, _vp, c_int, _sz, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp],
+    ),
+    "ks_b200_quantize_per_token_async": (c_int, [_vp, _sz, _sz, _sz, _vp, _sz, _vp, _vp]),
+    # include/ks_b200_ggml.h: the GGML MUL_MAT(Q4_0, f32) adapter
+    "ks_b200_ggml_q4_0_create": (c_int, [_vp, _sz, _sz, _sz, _vp, _vp]),
+    "ks_b200_ggml_q4_0_destroy": (c_int, [_vp]),
+    "ks_b200_ggml_q4_0_native": (c_int, [_vp, _vp, _vp, _vp, _vp]),
+    "ks_b200_ggml_mul_mat_q4_0_async": (c_int, [_vp, _vp, _sz, _vp, _sz, _sz, _vp, _vp]),
+    "ks_b200_ggml_report_get": (None, [_vp]),
+    "ks_b200_ggml_report_reset": (None, []),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -234,6 +246,67 @@ def import_ggml_q4_0_async(blocks, block_row_stride, rows, cols, group, packed, 
             scale_type, scale_stride or cols // group, stream_handle(stream),
         )
     )
+
+
+def matvec_w4a8_f32in_async(x, w, w_stride, s, s_stride, y, rows, cols, group, scale_type=SCALE_F16, xq=None,
+                            xs=None, status=None, stream=None) -> None:
+    """W4A8 GEMV on f32 activations, quantised per token on the device."""
+    check(
+        lib().ks_b200_matvec_w4a8_f32in_async(
+            addr(x), addr(w), w_stride, addr(s), scale_type, s_stride, addr(y), rows, cols, group, addr(xq),
+            addr(xs), addr(status), stream_handle(stream),
+        )
+    )
+
+
+def quantize_per_token_async(x, ldx, n_tokens, cols, q, ldq, scales, stream=None) -> None:
+    """int8 per-token quantisation (s = max|x| / 127, round half to even)."""
+    check(lib().ks_b200_quantize_per_token_async(addr(x), ldx, n_tokens, cols, addr(q), ldq, addr(scales),
+                                                 stream_handle(stream)))
+
+
+class GgmlReport(ctypes.Structure):
+    """ks_b200_ggml_report (include/ks_b200_ggml.h)."""
+
+    _fields_ = [("conversions", ctypes.c_uint64), ("mul_mat_calls", ctypes.c_uint64), ("tokens", ctypes.c_uint64),
+                ("gemv_launches", ctypes.c_uint64), ("gemm_launches", ctypes.c_uint64)]
+
+
+def ggml_report() -> dict:
+    r = GgmlReport()
+    lib().ks_b200_ggml_report_get(ctypes.byref(r))
+    return {name: int(getattr(r, name)) for name, _ in GgmlReport._fields_}
+
+
+class GgmlQ4_0:
+    """A GGML Q4_0 weight converted once to the native W4A8 layout (device-resident),
+    multiplied through ks_b200_ggml_mul_mat_q4_0_async."""
+
+    def __init__(self, blocks, block_row_stride, rows, cols, stream=None):
+        h = c_void_p()
+        check(lib().ks_b200_ggml_q4_0_create(addr(blocks), block_row_stride, rows, cols, stream_handle(stream),
+                                             ctypes.byref(h)))
+        self.handle, self.rows, self.cols = h, rows, cols
+
+    def mul_mat_async(self, src1, src1_stride, dst, dst_stride, n_tokens, status=None, stream=None) -> None:
+        check(lib().ks_b200_ggml_mul_mat_q4_0_async(self.handle, addr(src1), src1_stride, addr(dst), dst_stride,
+                                                    n_tokens, addr(status), stream_handle(stream)))
+
+    def native(self):
+        p, s = c_void_p(), c_void_p()
+        check(lib().ks_b200_ggml_q4_0_native(self.handle, ctypes.byref(p), ctypes.byref(s), None, None))
+        return p.value, s.value
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib().ks_b200_ggml_q4_0_destroy(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def _ptr_array(objs):
