@@ -572,7 +572,7 @@ def run_decode_layers(K, torch, dev, args):
     peak, _ = measured_hbm_peak()
     b = layer_bytes()
     return {"layers": n, "us_per_layer": us, "weight_bytes_per_layer": b, "GB_s": b / us / 1e3,
-            "frac": b / us / 1e3 / peak, "launches_per_layer": 4,
+            "frac": b / us / 1e3 / peak, "launches_per_layer": L.ks_b200_decode_layer_launches(h, i, GROUP),
             "shape": "hidden 4096, inter 11008, W4A8 G32 f16 scales, batch 1, fused RMSNorm/quantise/SiLU/residual"}
 
 

@@ -269,6 +269,10 @@ int ks_b200_peer_arrival_wait_async(const uint32_t *counter,
  * again before reusing it.
  */
 size_t ks_b200_decode_layer_workspace(size_t hidden, size_t inter);
+/* Kernel launches one ks_b200_decode_layer_w4a8_async call of this shape
+ * makes on the current device (16-byte aligned operands): 1 for the
+ * persistent kernel, 4 for the chained fallback, 0 for an invalid shape. */
+int ks_b200_decode_layer_launches(size_t hidden, size_t inter, size_t group_size);
 int ks_b200_decode_layer_offsets(size_t hidden, size_t inter, size_t *offsets);
 int ks_b200_decode_layer_w4a8_async(const float *h_in, float *h_out,
                                     const float *norm1_w, const float *norm2_w,

@@ -58,6 +58,7 @@ def layer(request, cuda, ks):
                                                        dn2.data_ptr(), EPS, wptr, sptr, H, I, G, ws.data_ptr(),
                                                        ws_bytes, status.data_ptr(), ks.stream_handle(stream)))
             stream.synchronize()
+            launches.append(L.ks_b200_decode_layer_launches(H, I, G))
         finally:
             if old is None:
                 del os.environ["KS_B200_DECODE_PERSISTENT"]
@@ -65,6 +66,7 @@ def layer(request, cuda, ks):
                 os.environ["KS_B200_DECODE_PERSISTENT"] = old
         return out.cpu().numpy().copy(), ws.cpu().numpy().copy()
 
+    launches = []
     y1, w1 = run()
     y2, w2 = run()
     offs = (ctypes.c_size_t * 12)()
@@ -82,7 +84,8 @@ def layer(request, cuda, ks):
     # barrier words (a generation counter that advances every call)
     for w in (w1, w2):
         w[o[6] + 128:o[6] + 256] = 0
-    return dict(W=W, S=S, h=h, n1=n1, n2=n2, gpu=gpu, y2=y2, w2=w2, w1=w1, status=status.cpu().tolist())
+    return dict(W=W, S=S, h=h, n1=n1, n2=n2, gpu=gpu, y2=y2, w2=w2, w1=w1, status=status.cpu().tolist(),
+                launches=launches, path=request.param)
 
 
 def _close(y, ref, what):
@@ -98,6 +101,8 @@ def _gemv(oracle, layer, k, q, s, rows, cols):
 
 def test_status_and_determinism(layer):
     assert layer["status"] == [0, 0]
+    # the path query agrees with the path the fixture forced
+    assert layer["launches"] == [1, 1] if layer["path"] == "persistent" else layer["launches"] == [4, 4]
     np.testing.assert_array_equal(layer["gpu"]["h_out"].view(np.uint32), layer["y2"].view(np.uint32))
     np.testing.assert_array_equal(layer["w1"], layer["w2"])
 

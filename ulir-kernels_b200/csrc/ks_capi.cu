@@ -1018,3 +1018,25 @@ extern "C" int ks_b200_decode_layer_w4a8_async(const float *h_in, float *h_out, 
     return fail(KS_ERR_UNSUPPORTED, "decode layer needs 16-byte aligned weights/scales and the streaming shape");
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
 }
+
+extern "C" int ks_b200_decode_layer_launches(size_t hidden, size_t inter, size_t group_size) {
+  if (hidden == 0 || inter == 0 || hidden % 32 || inter % 32 || group_size < 32 || group_size % 32 ||
+      (group_size & (group_size - 1)) || hidden % group_size || inter % group_size)
+    return 0;
+  int dev;
+  if (current_device(&dev) != KS_OK) return 0;
+  // 16-byte aligned stand-ins: the dry run checks addresses, never reads them
+  const auto *fake = reinterpret_cast<const uint8_t *>(uintptr_t(256));
+  DecodeLayerArgs a{};
+  a.h_in = a.norm1_w = a.norm2_w = reinterpret_cast<const float *>(fake);
+  for (int k = 0; k < 5; ++k) {
+    a.w[k] = fake;
+    a.s[k] = fake;
+  }
+  a.hidden = (int64_t)hidden;
+  a.inter = (int64_t)inter;
+  a.group = (int64_t)group_size;
+  const cudaError_t e = launch_decode_layer_persistent(a, nullptr, dev, /*dry=*/true);
+  cudaGetLastError();
+  return e == cudaSuccess ? 1 : 4;
+}

@@ -491,7 +491,7 @@ int ncpl_for(int64_t cols) {
 }
 
 template <int NH, int NI>
-cudaError_t launch_persistent(const DecParams &P, size_t smem, cudaStream_t stream, int device) {
+cudaError_t launch_persistent(const DecParams &P, size_t smem, cudaStream_t stream, int device, bool dry) {
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   static int fits[64];
@@ -507,6 +507,7 @@ cudaError_t launch_persistent(const DecParams &P, size_t smem, cudaStream_t stre
   });
   if (attr_err[device & 63] != cudaSuccess) return attr_err[device & 63];
   if (fits[device & 63] < 1) return cudaErrorNotSupported;
+  if (dry) return cudaSuccess;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)device_props(device).sm_count);
   cfg.blockDim = dim3(kDecThreads);
@@ -522,7 +523,7 @@ cudaError_t launch_persistent(const DecParams &P, size_t smem, cudaStream_t stre
 
 }  // namespace
 
-cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device) {
+cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device, bool dry) {
   if (env_int("KS_B200_DECODE_PERSISTENT", 1) == 0) return cudaErrorNotSupported;
   const int64_t h = a.hidden, i = a.inter, G = a.group;
   const int NH = ncpl_for(h), NI = ncpl_for(i);
@@ -585,9 +586,9 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
   for (int k = 0; k < 4; ++k) P.q[k] = a.q[k];
   P.status = a.status;
   const size_t smem = (size_t)kBarBytes + xbuf + (size_t)nslots * slot;
-  if (NH == 4 && NI == 12) return launch_persistent<4, 12>(P, smem, stream, device);
-  if (NH == 4 && NI == 16) return launch_persistent<4, 16>(P, smem, stream, device);
-  return launch_persistent<8, 16>(P, smem, stream, device);
+  if (NH == 4 && NI == 12) return launch_persistent<4, 12>(P, smem, stream, device, dry);
+  if (NH == 4 && NI == 16) return launch_persistent<4, 16>(P, smem, stream, device, dry);
+  return launch_persistent<8, 16>(P, smem, stream, device, dry);
 }
 
 }  // namespace ksb

@@ -134,7 +134,9 @@ cudaError_t launch_decode_layer_w4a8(const DecodeLayerArgs &a, cudaStream_t stre
 // The same layer as one cooperative persistent kernel; cudaErrorNotSupported
 // when the shape, the alignment or the device does not allow it (the caller
 // then uses the four-launch path).
-cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device);
+// dry: every check (shape, alignment, occupancy), no launch
+cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device,
+                                           bool dry = false);
 
 // Wait (bounded) until *counter reaches expected[0] + arrivals; expected[0]
 // then holds the new target.

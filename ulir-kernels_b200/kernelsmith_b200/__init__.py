@@ -123,6 +123,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _vp, _sz, _vp, c_int, _sz, _vp, _sz, _sz, _sz, _vp, _vp, _vp, _vp],
     ),
     "ks_b200_quantize_per_token_async": (c_int, [_vp, _sz, _sz, _sz, _vp, _sz, _vp, _vp]),
+    "ks_b200_decode_layer_launches": (c_int, [_sz, _sz, _sz]),
     # include/ks_b200_ggml.h: the GGML MUL_MAT(Q4_0, f32) adapter
     "ks_b200_ggml_q4_0_create": (c_int, [_vp, _sz, _sz, _sz, _vp, _vp]),
     "ks_b200_ggml_q4_0_destroy": (c_int, [_vp]),
