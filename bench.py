@@ -657,10 +657,23 @@ def run_gemm(K, torch, dev):
             for i in range(32):
                 K.gemm_i8_requant_async(A, sa, W[i % copies], ws, 0.05, o, M, N, Kd, status=status, stream=stream)
 
+        outs = [torch.zeros((M, N), dtype=torch.int8, device=dev) for _ in range(16)]
+
+        def fn_batched():
+            # the same 32 GEMMs as two batched launches of 16
+            for c in range(2):
+                ids = range(16 * c, 16 * c + 16)
+                K.gemm_i8_requant_batch_async([A] * 16, [sa] * 16, [W[i % copies] for i in ids], [ws] * 16, 0.05,
+                                              outs, M, N, Kd, status=status, stream=stream)
+
         us = _graph_us(torch, stream, fn, 32, reps=5)
+        us_b = _graph_us(torch, stream, fn_batched, 32, reps=5)
         assert status.cpu().tolist() == [0, 0]
         b = N * Kd + M * Kd + M * N + 4 * (M + N)
-        out[f"M{M}"] = {"us": us, "TB_s": b / us / 1e6, "frac": b / us / 1e3 / peak}
+        out[f"M{M}"] = {"us": us, "TB_s": b / us / 1e6, "frac": b / us / 1e3 / peak,
+                        "batched_16": {"us": us_b, "TB_s": b / us_b / 1e6, "frac": b / us_b / 1e3 / peak}}
+    out["note"] = ("M<n>: one launch per GEMM (graph of 32, programmatic dependent launch); batched_16: the same "
+                   "32 GEMMs as two launches of ks_b200_gemm_i8_requant_batch_async")
     return out
 
 

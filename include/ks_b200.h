@@ -318,6 +318,27 @@ int ks_b200_gemm_i8_requant_async(const int8_t *a, size_t lda,
                                   void *stream);
 
 /*
+ * Batched form of ks_b200_gemm_i8_requant_async (no counterpart in the
+ * reference): `count` independent GEMMs of one shape, out_i = requant(a_i x
+ * w_i^T) with a_scales[i], w_scales[i] and the shared out_scale, each output
+ * bit-identical to the single call.  The pointer arrays are host memory
+ * holding device pointers.  With m <= 64 and every operand on the tensor-core
+ * path, up to 16 GEMMs run in one persistent launch: each SM streams its rows
+ * of every weight matrix back to back, and a GEMM's requantising epilogue
+ * overlaps the next GEMM's main loop; otherwise one launch per GEMM.  No
+ * allocation, capturable in a CUDA graph.
+ */
+int ks_b200_gemm_i8_requant_batch_async(int count, const int8_t *const *a,
+                                        size_t lda,
+                                        const float *const *a_scales,
+                                        const int8_t *const *w, size_t ldw,
+                                        const float *const *w_scales,
+                                        float out_scale, int8_t *const *out,
+                                        size_t ldo, size_t m, size_t n,
+                                        size_t k, uint32_t *status,
+                                        void *stream);
+
+/*
  * Which kernel family a W4A8 / INT8 call with these arguments runs on the
  * current device: 1 = TMA-staged streaming kernel, 0 = generic per-element
  * kernel (any stride, alignment, odd cols, any group size), negative = the

@@ -188,3 +188,124 @@ def test_gemm_requant_exact_ties(ks, cuda, oracle, out_scale):
     np.testing.assert_array_equal(out, out_ref)
     q = acc_ref.astype(np.float32) / np.float32(out_scale)
     assert (q - np.floor(q) == np.float32(0.5)).sum() > 100  # exact ties are present
+
+
+def _batch_inputs(torch, cuda, seed, count, m, n, k, shared_a=False):
+    dev = lambda x: torch.from_numpy(x).to(cuda)
+    cases = [_case(seed + 7 * i, m, n, k) for i in range(count)]
+    if shared_a:
+        cases = [(cases[0][0], w, cases[0][2], ws) for _, w, _, ws in cases]
+    A = [dev(c[0]) for c in cases]
+    W = [dev(c[1]) for c in cases]
+    SA = [dev(c[2]) for c in cases]
+    WS = [dev(c[3]) for c in cases]
+    return cases, A, W, SA, WS
+
+
+@pytest.mark.parametrize("m", [8, 16, 32, 64])
+def test_gemm_batch_matches_single_and_oracle(ks, cuda, oracle, m):
+    """Four GEMMs M x 4096 x 14336 in one batched launch: each output equals the
+    single-GEMM launch bit for bit and the oracle on a sample of weight rows."""
+    import torch
+
+    n, k, count = 14336, 4096, 4
+    cases, A, W, SA, WS = _batch_inputs(torch, cuda, 500 + m, count, m, n, k)
+    outs = [torch.zeros((m, n), dtype=torch.int8, device=cuda) for _ in range(count)]
+    status = torch.zeros(2, dtype=torch.int32, device=cuda)
+    ks.gemm_i8_requant_batch_async(A, SA, W, WS, 0.05, outs, m, n, k, status=status)
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    rows = np.unique(np.concatenate([np.arange(0, 128), np.arange(n - 128, n),
+                                     np.random.default_rng(m).choice(n, 256, replace=False)]))
+    for i, (a, w, sa, ws) in enumerate(cases):
+        single, _ = _run_async(ks, torch, cuda, a, w, sa, ws, 0.05)
+        got = outs[i].cpu().numpy()
+        np.testing.assert_array_equal(got, single)
+        rc, out_ref = oracle.gemm_i8_requant(a, sa, np.ascontiguousarray(w[rows]), ws[rows], 0.05)
+        assert rc == 0
+        np.testing.assert_array_equal(got[:, rows], out_ref)
+
+
+@pytest.mark.parametrize("shape,count", [((1, 128, 128), 3), ((5, 200, 320), 5), ((17, 1000, 1040), 2),
+                                         ((48, 384, 4224), 3), ((3, 129, 48), 18), ((64, 2000, 256), 17)])
+def test_gemm_batch_ragged_bit_exact(ks, cuda, oracle, shape, count):
+    """Ragged M, N and K; counts above 16 take more than one launch."""
+    import torch
+
+    m, n, k = shape
+    cases, A, W, SA, WS = _batch_inputs(torch, cuda, sum(shape) + count, count, m, n, k, shared_a=count % 2 == 1)
+    outs = [torch.zeros((m, n), dtype=torch.int8, device=cuda) for _ in range(count)]
+    status = torch.zeros(2, dtype=torch.int32, device=cuda)
+    ks.gemm_i8_requant_batch_async(A, SA, W, WS, 0.01, outs, m, n, k, status=status)
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    for i, (a, w, sa, ws) in enumerate(cases):
+        rc, out_ref = oracle.gemm_i8_requant(a, sa, w, ws, 0.01)
+        assert rc == 0
+        np.testing.assert_array_equal(outs[i].cpu().numpy(), out_ref)
+
+
+def test_gemm_batch_unaligned_output_and_strides(ks, cuda, oracle):
+    """An output row stride that is not a multiple of 16 takes the direct-store
+    epilogue; strided outputs keep their gaps."""
+    import torch
+
+    m, n, k, count, ldo = 9, 520, 512, 3, 530
+    cases, A, W, SA, WS = _batch_inputs(torch, cuda, 901, count, m, n, k)
+    bufs = [torch.full((m * ldo,), 99, dtype=torch.int8, device=cuda) for _ in range(count)]
+    ks.gemm_i8_requant_batch_async(A, SA, W, WS, 0.03, bufs, m, n, k, ldo=ldo)
+    torch.cuda.synchronize()
+    for i, (a, w, sa, ws) in enumerate(cases):
+        rc, out_ref = oracle.gemm_i8_requant(a, sa, w, ws, 0.03)
+        o = bufs[i].cpu().numpy().reshape(m, ldo)
+        np.testing.assert_array_equal(o[:, :n], out_ref)
+        assert (o[:, n:] == 99).all()
+
+
+def test_gemm_batch_chain_on_side_stream(ks, cuda, oracle):
+    """Two batched launches on one stream, the second reading the first's int8
+    outputs as its activations (programmatic dependent launch on)."""
+    import torch
+
+    m, k, count = 16, 2048, 3
+    g = np.random.default_rng(321)
+    a0 = [g.integers(-127, 128, (m, k), dtype=np.int8) for _ in range(count)]
+    w1 = [g.integers(-127, 128, (k, k), dtype=np.int8) for _ in range(count)]
+    w2 = [g.integers(-127, 128, (k, k), dtype=np.int8) for _ in range(count)]
+    ws = [g.uniform(1e-3, 1e-2, k).astype(np.float32) for _ in range(count)]
+    sa = np.full(m, 1.1e-3, np.float32)
+    dev = lambda x: torch.from_numpy(x).to(cuda)
+    stream = torch.cuda.Stream(device=cuda)
+    mid = [torch.zeros((m, k), dtype=torch.int8, device=cuda) for _ in range(count)]
+    fin = [torch.zeros((m, k), dtype=torch.int8, device=cuda) for _ in range(count)]
+    DA, DW1, DW2, DWS = [dev(x) for x in a0], [dev(x) for x in w1], [dev(x) for x in w2], [dev(x) for x in ws]
+    DSA = [dev(sa) for _ in range(count)]
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        ks.gemm_i8_requant_batch_async(DA, DSA, DW1, DWS, 0.05, mid, m, k, k, stream=stream)
+        ks.gemm_i8_requant_batch_async(mid, DSA, DW2, DWS, 0.05, fin, m, k, k, stream=stream)
+    stream.synchronize()
+    for i in range(count):
+        rc, r1 = oracle.gemm_i8_requant(a0[i], sa, w1[i], ws[i], 0.05)
+        rc, r2 = oracle.gemm_i8_requant(r1, sa, w2[i], ws[i], 0.05)
+        np.testing.assert_array_equal(fin[i].cpu().numpy(), r2)
+        assert len(np.unique(r2)) > 20
+
+
+def test_gemm_batch_rejects_bad_args(ks, cuda):
+    import torch
+
+    L = ks.lib()
+    a = torch.zeros((4, 64), dtype=torch.int8, device=cuda)
+    s = torch.ones(64, dtype=torch.float32, device=cuda)
+    o = torch.zeros((4, 64), dtype=torch.int8, device=cuda)
+    arr = lambda *t: ks._ptr_array(list(t))
+    E = ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_gemm_i8_requant_batch_async(-1, None, 64, None, None, 64, None, 1.0, None, 64, 4, 64, 64,
+                                                 None, None) == E
+    assert L.ks_b200_gemm_i8_requant_batch_async(2, arr(a, a), 64, arr(s, s), arr(a, a), 64, arr(s, s), 0.0,
+                                                 arr(o, o), 64, 4, 64, 64, None, None) == E
+    assert L.ks_b200_gemm_i8_requant_batch_async(2, arr(a, a), 64, arr(s, s), arr(a, None), 64, arr(s, s), 1.0,
+                                                 arr(o, o), 64, 4, 64, 64, None, None) == E
+    assert L.ks_b200_gemm_i8_requant_batch_async(0, None, 64, None, None, 64, None, 1.0, None, 64, 4, 64, 64,
+                                                 None, None) == ks.KS_OK

@@ -751,6 +751,34 @@ extern "C" int ks_b200_gemm_i8_requant_async(const int8_t *a, size_t lda, const 
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
 }
 
+extern "C" int ks_b200_gemm_i8_requant_batch_async(int count, const int8_t *const *a, size_t lda,
+                                                   const float *const *a_scales, const int8_t *const *w,
+                                                   size_t ldw, const float *const *w_scales, float out_scale,
+                                                   int8_t *const *out, size_t ldo, size_t m, size_t n, size_t k,
+                                                   uint32_t *status, void *stream) {
+  if (count < 0 || (count > 0 && (!a || !a_scales || !w || !w_scales || !out)))
+    return fail(KS_ERR_INVALID_ARG, "bad batch arrays");
+  for (int i = 0; i < count; ++i) {
+    const int rc = gemm_checks(a[i], lda, a_scales[i], w[i], ldw, w_scales[i], out_scale, out[i], ldo, m, n, k);
+    if (rc != KS_OK) return rc;
+  }
+  if (count == 0) return KS_OK;
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  GemmI8Launch g{};
+  g.lda = (int64_t)lda;
+  g.ldw = (int64_t)ldw;
+  g.out_scale = out_scale;
+  g.ldo = (int64_t)ldo;
+  g.m = (int64_t)m;
+  g.n = (int64_t)n;
+  g.k = (int64_t)k;
+  g.status = status;
+  GemmI8Batch b{count, a, a_scales, w, w_scales, out};
+  cudaError_t e = launch_gemm_i8_batch(g, b, static_cast<cudaStream_t>(stream), dev);
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
 extern "C" int ks_b200_gemm_i8_kernel_path(const void *a, size_t lda, const void *w, size_t ldw, size_t m,
                                            size_t n, size_t k) {
   if (m == 0 || n == 0 || k == 0 || lda < k || ldw < k) return -1;

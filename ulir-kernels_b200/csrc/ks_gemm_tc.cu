@@ -325,6 +325,251 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------
+// Batched form: `count` independent GEMMs of the same shape in one launch.
+// Every CTA owns the same tile_rows weight rows of every GEMM and streams
+// them GEMM after GEMM through one stage ring, so the ring never drains
+// between GEMMs and the launch, ramp-up and tail are paid once per launch
+// instead of once per GEMM.  The accumulator is double-buffered in TMEM
+// (2 x mpad columns): the epilogue requantises and stores GEMM i from one
+// buffer while the MMA warp accumulates GEMM i + 1 into the other.  The
+// int8 output tile has its own shared-memory buffer (the ring is still in
+// use), stored by one TMA store per GEMM whose shared-memory reads are waited
+// for before the next GEMM's tile is written.
+constexpr int kMaxGemmItems = 16;
+constexpr int kBatchMaxTokens = 64;
+constexpr int kBatchTileBytes = kBatchMaxTokens * kMmaRows;  // int8 output tile [mpad x tile_rows]
+
+struct GemmBatchMaps {  // tensor maps live in the kernel's parameter space
+  CUtensorMap w[kMaxGemmItems];
+  CUtensorMap a[kMaxGemmItems];
+  CUtensorMap o[kMaxGemmItems];
+};
+
+struct GemmBatchParams {
+  const float *sa[kMaxGemmItems];
+  const float *ws[kMaxGemmItems];
+  int8_t *out[kMaxGemmItems];
+  float out_scale;
+  float inv_out_scale;
+  int64_t ldo;
+  int32_t count, m, n, k;
+  int32_t mpad, nkb, nst, stage_bytes, b_bytes, tile_rows, tma_store;
+  uint32_t tmem_cols;
+  uint32_t *status;
+};
+
+__device__ __forceinline__ void tma_store_2d_commit(const CUtensorMap *map, int x, int y, const void *src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+               "r"(y), "r"(smem_u32(src))
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_i8_tc_batch_kernel(const __grid_constant__ GemmBatchMaps maps, const GemmBatchParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // [ring: nst stages] [int8 output tile] [barriers ...] [activation scales, two buffers]
+  uint8_t *stages = smem;
+  int8_t *tile = reinterpret_cast<int8_t *>(smem + (size_t)p.nst * p.stage_bytes);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)p.nst * p.stage_bytes + kBatchTileBytes);
+  uint64_t *empty = full + p.nst;
+  uint64_t *acc_full = empty + p.nst;  // [2] accumulator buffer complete
+  uint64_t *acc_empty = acc_full + 2;  // [2] accumulator buffer read by the epilogue
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+  float *sa_buf = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(full) + kBarRegion);  // [2][64]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * p.tile_rows;
+  const int total = p.count * p.nkb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiThreads / 32);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(p.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer --
+    if (lane == 0) {
+      for (int i = 0; i < p.count; ++i) {
+        prefetch_tmap(&maps.w[i]);
+        prefetch_tmap(&maps.a[i]);
+      }
+      const uint64_t pol = l2_policy_evict_first();
+      const uint32_t tx = (uint32_t)(p.tile_rows * kKBlock + p.b_bytes);
+      const int pre = min(p.nst, total);
+      // weights of the first stages, before the previous grid has finished
+      for (int gs = 0; gs < pre; ++gs) {
+        mbar_arrive_expect_tx(&full[gs], tx);
+        tma_load_2d_hint(stages + (size_t)gs * p.stage_bytes, &maps.w[gs / p.nkb], (gs % p.nkb) * kKBlock, row0,
+                         &full[gs], pol);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int gs = 0; gs < pre; ++gs)
+        tma_load_2d(stages + (size_t)gs * p.stage_bytes + kWTileBytes, &maps.a[gs / p.nkb], (gs % p.nkb) * kKBlock,
+                    0, &full[gs]);
+      int issued = pre;
+      for (int gs = pre; gs < total; ++gs) {
+        const int s = gs % p.nst, i = gs / p.nkb, kb = gs % p.nkb;
+        if (!mbar_wait(&empty[s], (uint32_t)((gs / p.nst) - 1) & 1u)) {
+          set_status(p.status, kStatusTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t *st = stages + (size_t)s * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[s], tx);
+        tma_load_2d_hint(st, &maps.w[i], kb * kKBlock, row0, &full[s], pol);
+        tma_load_2d(st + kWTileBytes, &maps.a[i], kb * kKBlock, 0, &full[s]);
+        ++issued;
+      }
+      for (int gs = max(0, issued - p.nst); gs < issued; ++gs) {
+        if (!mbar_wait(&full[gs % p.nst], (uint32_t)(gs / p.nst) & 1u)) set_status(p.status, kStatusTimeout);
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA issuer --
+    if (lane == 0) {
+      const uint32_t idesc = (2u << 4)                            // D: s32
+                             | (1u << 7) | (1u << 10)             // A, B: signed int8
+                             | ((uint32_t)(p.mpad >> 3) << 17)    // N
+                             | ((uint32_t)(kMmaRows >> 4) << 24);  // M
+      int gs = 0;
+      bool stop = false;
+      for (int i = 0; i < p.count && !stop; ++i) {
+        const int b = i & 1;
+        // the epilogue has read this buffer's previous GEMM (i - 2)
+        if (i >= 2 && !mbar_wait(&acc_empty[b], (uint32_t)((i >> 1) - 1) & 1u)) {
+          set_status(p.status, kStatusTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_d + (uint32_t)(b * p.mpad);
+        for (int kb = 0; kb < p.nkb; ++kb, ++gs) {
+          const int s = gs % p.nst;
+          if (!mbar_wait(&full[s], (uint32_t)(gs / p.nst) & 1u)) {
+            set_status(p.status, kStatusTimeout);
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          uint8_t *st = stages + (size_t)s * p.stage_bytes;
+          const uint64_t adesc = umma_desc_sw128(st);
+          const uint64_t bdesc = umma_desc_sw128(st + kWTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kKBlock / 32; ++kk)
+            tc_mma_i8(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&empty[s]);
+        }
+        if (!stop) tc_commit(&acc_full[b]);  // fires once GEMM i's MMAs have completed
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue --
+    const int et = threadIdx.x - 64;  // 0..127
+    const int quarter = warp & 3;     // TMEM lanes 32*quarter .. +31
+    const int r = quarter * 32 + lane;
+    const int n = row0 + r;
+    const bool row_ok = r < p.tile_rows && n < p.n;
+    const bool via_tma = p.tma_store != 0;
+    // Scales may come from the previous grid; outputs may still be read by it.
+    pdl_wait();
+    const uint32_t taddr0 = tmem_d + ((uint32_t)(quarter * 32) << 16);
+    bool stored = false;
+    for (int i = 0; i < p.count; ++i) {
+      const int b = i & 1;
+      float *sa_s = sa_buf + b * kBatchMaxTokens;
+      const float *__restrict__ sa = p.sa[i];
+      for (int m = et; m < p.mpad; m += kEpiThreads) sa_s[m] = m < p.m ? sa[m] : 0.0f;
+      const float wsn = row_ok ? p.ws[i][n] : 0.0f;
+      // sa_s is complete, and thread 0 has seen the previous tile's store read
+      epi_barrier();
+      const bool ok = epi_all(mbar_wait(&acc_full[b], (uint32_t)(i >> 1) & 1u));
+      tc_fence_after();
+      if (!ok) {
+        if (et == 0) set_status(p.status, kStatusTimeout);
+        break;
+      }
+      if (!epi_all(*abort_flag == 0)) break;
+      int8_t *__restrict__ out = p.out[i];
+      const uint32_t taddr = taddr0 + (uint32_t)(b * p.mpad);
+      for (int c0 = 0; c0 < p.mpad; c0 += 32) {
+        const bool two = c0 + 16 < p.mpad;  // uniform across the CTA
+        uint32_t va[16], vb[16];
+        tc_ld16_nowait(taddr + (uint32_t)c0, va);
+        if (two) tc_ld16_nowait(taddr + (uint32_t)(c0 + 16), vb);
+        tc_wait_ld(va, vb);
+        int oa[16], ob[16];
+        requant16(va, sa_s + c0, wsn, p.out_scale, p.inv_out_scale, oa);
+        if (two) requant16(vb, sa_s + c0 + 16, wsn, p.out_scale, p.inv_out_scale, ob);
+        for (int h = 0; h < (two ? 2 : 1); ++h) {
+          const int cb = c0 + 16 * h;
+          const int(&o)[16] = h ? ob : oa;
+          if (via_tma) {
+            if (r < p.tile_rows) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) tile[(cb + j) * p.tile_rows + r] = (int8_t)o[j];
+            }
+          } else if (row_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (cb + j < p.m) out[(int64_t)(cb + j) * p.ldo + n] = (int8_t)o[j];
+          }
+        }
+      }
+      // this warp's TMEM loads are complete (tcgen05.wait::ld above): free the buffer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (via_tma) {
+        // generic-proxy writes of the tile -> visible to the bulk-copy engine
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        epi_barrier();
+        // rows >= m and columns >= n fall outside the tensor and are not written
+        if (et == 0) {
+          tma_store_2d_commit(&maps.o[i], row0, 0, tile);
+          bulk_wait_read_all();  // the tile may be rewritten after the next barrier
+          stored = true;
+        }
+      }
+    }
+    if (stored) bulk_wait_all();  // every output store has completed before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(p.tmem_cols)
+                 : "memory");
+  }
+}
+
 // Generic fallback (any strides / alignment): one warp per (token, weight row).
 __global__ void __launch_bounds__(256)
     gemm_i8_generic_kernel(const int8_t *__restrict__ a, int64_t lda, const int8_t *__restrict__ w, int64_t ldw,
@@ -432,6 +677,104 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
     cfg.numAttrs = 1;
   }
   return cudaLaunchKernelEx(&cfg, gemm_i8_tc_kernel, mw, ma, mo, p);
+}
+
+cudaError_t launch_gemm_i8_batch(const GemmI8Launch &shape, const GemmI8Batch &b, cudaStream_t stream,
+                                 int device) {
+  if (b.count <= 0) return cudaSuccess;
+  auto item = [&](int i) {
+    GemmI8Launch g = shape;
+    g.a = b.a[i];
+    g.sa = b.sa[i];
+    g.w = b.w[i];
+    g.ws = b.ws[i];
+    g.out = b.out[i];
+    g.acc_out = nullptr;
+    return g;
+  };
+  // The batched kernel takes up to 64 tokens with every operand on the
+  // tensor-core path; anything else runs one launch per GEMM.
+  bool batched = shape.m <= kBatchMaxTokens;
+  for (int i = 0; i < b.count && batched; ++i) batched = tc_shape_ok(item(i));
+  if (!batched) {
+    for (int i = 0; i < b.count; ++i) {
+      const cudaError_t e = launch_gemm_i8(item(i), stream, device);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+  const DeviceProps &dp = device_props(device);
+  GemmBatchParams p{};
+  p.out_scale = shape.out_scale;
+  {
+    const float inv = 1.0f / shape.out_scale;  // IEEE division on the host: RN(1 / out_scale)
+    p.inv_out_scale = std::isfinite(inv) ? inv : 0.0f;
+  }
+  p.ldo = shape.ldo;
+  p.m = (int32_t)shape.m;
+  p.n = (int32_t)shape.n;
+  p.k = (int32_t)shape.k;
+  p.status = shape.status;
+  p.mpad = (int32_t)((shape.m + 15) / 16 * 16);
+  p.nkb = (int32_t)((shape.k + kKBlock - 1) / kKBlock);
+  p.b_bytes = p.mpad * kKBlock;
+  p.stage_bytes = kWTileBytes + p.b_bytes;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * p.mpad)) cols <<= 1;
+  p.tmem_cols = cols;
+  const int64_t slots = (int64_t)dp.sm_count;
+  const int64_t waves = (shape.n + slots * kMmaRows - 1) / (slots * kMmaRows);
+  const int64_t even = (shape.n + waves * slots - 1) / (waves * slots);
+  const int64_t floor_rows = std::min<int64_t>(kMmaRows, std::max<int64_t>(16, p.mpad / 2));
+  p.tile_rows = (int32_t)std::min<int64_t>(kMmaRows, (std::max(even, floor_rows) + 15) / 16 * 16);
+  const int grid = (int)((shape.n + p.tile_rows - 1) / p.tile_rows);
+  const int reserve = 1024 /* alignment slack */ + kBatchTileBytes + kBarRegion + 2 * kBatchMaxTokens * 4;
+  int nst_cap = (dp.smem_optin - reserve) / p.stage_bytes;
+  nst_cap = std::min(nst_cap, std::max(1, std::min(kMaxStages, env_int("KS_B200_GEMM_STAGES", 8))));
+  if (nst_cap < 1) return cudaErrorInvalidValue;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[device & 63], [&] {
+    attr_err[device & 63] =
+        cudaFuncSetAttribute(gemm_i8_tc_batch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dp.smem_optin);
+  });
+  if (attr_err[device & 63] != cudaSuccess) return attr_err[device & 63];
+  for (int i0 = 0; i0 < b.count; i0 += kMaxGemmItems) {
+    const int cnt = std::min(kMaxGemmItems, b.count - i0);
+    GemmBatchMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    p.count = cnt;
+    p.nst = std::min<int>(nst_cap, cnt * p.nkb);
+    bool tma_store = shape.ldo % 16 == 0;
+    for (int j = 0; j < cnt; ++j) {
+      const int i = i0 + j;
+      p.sa[j] = b.sa[i];
+      p.ws[j] = b.ws[i];
+      p.out[j] = b.out[i];
+      if (!make_map(&maps.w[j], b.w[i], shape.n, shape.k, shape.ldw, p.tile_rows) ||
+          !make_map(&maps.a[j], b.a[i], shape.m, shape.k, shape.lda, p.mpad))
+        return cudaErrorInvalidValue;
+      tma_store = tma_store && (reinterpret_cast<uintptr_t>(b.out[i]) & 15u) == 0 &&
+                  make_store_map(&maps.o[j], b.out[i], shape.m, shape.n, shape.ldo, p.tile_rows, p.mpad);
+    }
+    p.tma_store = tma_store ? 1 : 0;
+    const size_t smem = (size_t)reserve + (size_t)p.nst * p.stage_bytes;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (pdl_enabled(stream)) {
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8_tc_batch_kernel, maps, p);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace ksb

@@ -144,6 +144,19 @@ cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32
                              cudaStream_t stream);
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
 
+// Independent GEMMs of one shape (m, n, k, strides and out_scale from the
+// GemmI8Launch; its pointers are unused): host arrays of device pointers.
+struct GemmI8Batch {
+  int count;
+  const int8_t *const *a;
+  const float *const *sa;
+  const int8_t *const *w;
+  const float *const *ws;
+  int8_t *const *out;
+};
+cudaError_t launch_gemm_i8_batch(const GemmI8Launch &shape, const GemmI8Batch &b, cudaStream_t stream,
+                                 int device);
+
 // Batched W4A8 GEMM (tokens x native int4 weights, group scales) on tcgen05.
 struct GemmW4A8Launch {
   const int8_t *a;      // [m, k] int8, row stride lda

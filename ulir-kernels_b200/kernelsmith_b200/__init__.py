@@ -110,6 +110,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz, _vp, _vp, _vp],
     ),
     "ks_b200_gemm_i8_kernel_path": (c_int, [_vp, _sz, _vp, _sz, _sz, _sz, _sz]),
+    "ks_b200_gemm_i8_requant_batch_async": (
+        c_int,
+        [c_int, _vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz, _vp, _vp],
+    ),
     "ks_b200_quant_layout_version": (c_int, []),
     "ks_b200_gemm_w4a8_async": (
         c_int,
@@ -223,6 +227,21 @@ def gemm_i8_requant_async(a, sa, w, ws, out_scale, out, m, n, k, lda=None, ldw=N
         lib().ks_b200_gemm_i8_requant_async(
             addr(a), lda or k, addr(sa), addr(w), ldw or k, addr(ws), out_scale, addr(out), ldo or n, m, n, k,
             addr(acc_out), addr(status), stream_handle(stream),
+        )
+    )
+
+
+def gemm_i8_requant_batch_async(a, sa, w, ws, out_scale, out, m, n, k, lda=None, ldw=None, ldo=None,
+                                status=None, stream=None) -> None:
+    """count independent INT8 GEMMs with requantisation (lists of device tensors)."""
+    count = len(w)
+    if not (len(a) == len(sa) == len(ws) == len(out) == count):
+        raise ValueError("batch lists differ in length")
+    check(
+        lib().ks_b200_gemm_i8_requant_batch_async(
+            count, _ptr_array(a), lda or k, _ptr_array(sa), _ptr_array(w), ldw or k, _ptr_array(ws), out_scale,
+            _ptr_array(out), ldo or n, m, n, k,
+            addr(status), stream_handle(stream),
         )
     )
 
