@@ -20,12 +20,16 @@
 // Warp-specialised CTA of 192 threads:
 //   warp 0  TMA producer: per 128-byte K block, one 2-D tiled copy of the
 //           weight tile [tile_rows x 128 B] and one of the activation tile
-//           [Mpad x 128 B], both 128-byte swizzled, into a ring of stages.
+//           [Mpad x 128 B], both 128-byte swizzled, into a ring of stages of
+//           up to four K blocks each (one barrier pair and one commit per
+//           stage: each producer -> MMA -> commit -> producer round trip costs
+//           a few hundred cycles of the MMA thread's time, so a stage carries
+//           16 MMAs rather than 4).
 //           The weight copies of the first stages are issued before
 //           griddepcontrol.wait (weights are never written by the kernels of
 //           this library that trigger an early launch); the activations only
 //           after it.  No multicast anywhere.
-//   warp 1  allocates TMEM, issues 4 x tcgen05.mma (K = 32 each) per stage,
+//   warp 1  allocates TMEM, issues 4 x tcgen05.mma (K = 32 each) per K block,
 //           frees the stage with tcgen05.commit, finally commits to the
 //           accumulator barrier; deallocates TMEM at the end.
 //   warps 2-5 epilogue: after griddepcontrol.wait, stage the per-token
@@ -66,6 +70,15 @@ constexpr int kWTileBytes = kMmaRows * kKBlock;  // weight region of a stage (MM
 constexpr int kBarRegion = 1024;                 // barriers, TMEM slot, abort flag
 constexpr int kScaleRegion = kMaxTokens * 4;     // activation scales
 
+// A stage holds `bps` consecutive K blocks: their weight tiles first (one
+// 16 KB MMA-A region each), then their activation tiles.  More blocks per
+// stage means fewer mbarrier round trips (TMA -> MMA -> commit -> producer)
+// per MMA; each round trip, not the MMA instruction, paces a skinny GEMM.
+__device__ __forceinline__ uint8_t *stage_w(uint8_t *st, int j) { return st + (size_t)j * kWTileBytes; }
+__device__ __forceinline__ uint8_t *stage_a(uint8_t *st, int bps, int b_bytes, int j) {
+  return st + (size_t)bps * kWTileBytes + (size_t)j * b_bytes;
+}
+
 struct GemmParams {
   const float *sa;
   const float *ws;
@@ -76,10 +89,12 @@ struct GemmParams {
   int32_t *acc_out;  // optional
   int32_t m, n, k;
   int32_t mpad;       // tokens padded to a multiple of 16
-  int32_t nkb;        // K blocks
-  int32_t nst;        // stages
+  int32_t nkb;        // K blocks of 128
+  int32_t bps;        // K blocks per stage (one barrier pair and one commit per stage)
+  int32_t nks;        // stages per GEMM: nkb / bps, rounded up
+  int32_t nst;        // ring stages
   int32_t stage_bytes;
-  int32_t b_bytes;    // activation tile bytes per stage
+  int32_t b_bytes;    // activation tile bytes per K block
   int32_t tile_rows;  // weight rows per CTA (TMA box height, multiple of 16, <= 128)
   int32_t tma_store;  // 1: the int8 tile leaves through one TMA store (aligned out, ldo)
   uint32_t tmem_cols;
@@ -193,33 +208,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_a);
       const uint64_t pol = l2_policy_evict_first();
-      const uint32_t tx = (uint32_t)(p.tile_rows * kKBlock + p.b_bytes);
-      const int pre = min(p.nst, p.nkb);
+      const uint32_t tx_block = (uint32_t)(p.tile_rows * kKBlock + p.b_bytes);
+      const int pre = min(p.nst, p.nks);
       // weights of the first stages, before the previous grid has finished
-      for (int kb = 0; kb < pre; ++kb) {
-        mbar_arrive_expect_tx(&full[kb], tx);
-        tma_load_2d_hint(stages + (size_t)kb * p.stage_bytes, &tmap_w, kb * kKBlock, row0, &full[kb], pol);
+      for (int ks = 0; ks < pre; ++ks) {
+        const int nb = min(p.bps, p.nkb - ks * p.bps);
+        uint8_t *st = stages + (size_t)ks * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[ks], (uint32_t)nb * tx_block);
+        for (int j = 0; j < nb; ++j)
+          tma_load_2d_hint(stage_w(st, j), &tmap_w, (ks * p.bps + j) * kKBlock, row0, &full[ks], pol);
       }
       pdl_wait();
       pdl_trigger();
-      for (int kb = 0; kb < pre; ++kb)
-        tma_load_2d(stages + (size_t)kb * p.stage_bytes + kWTileBytes, &tmap_a, kb * kKBlock, 0, &full[kb]);
+      for (int ks = 0; ks < pre; ++ks) {
+        const int nb = min(p.bps, p.nkb - ks * p.bps);
+        uint8_t *st = stages + (size_t)ks * p.stage_bytes;
+        for (int j = 0; j < nb; ++j)
+          tma_load_2d(stage_a(st, p.bps, p.b_bytes, j), &tmap_a, (ks * p.bps + j) * kKBlock, 0, &full[ks]);
+      }
       int issued = pre;
-      for (int kb = pre; kb < p.nkb; ++kb) {
-        const int s = kb % p.nst;
-        if (!mbar_wait(&empty[s], (uint32_t)((kb / p.nst) - 1) & 1u)) {
+      for (int ks = pre; ks < p.nks; ++ks) {
+        const int s = ks % p.nst;
+        if (!mbar_wait(&empty[s], (uint32_t)((ks / p.nst) - 1) & 1u)) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
+        const int nb = min(p.bps, p.nkb - ks * p.bps);
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d_hint(st, &tmap_w, kb * kKBlock, row0, &full[s], pol);
-        tma_load_2d(st + kWTileBytes, &tmap_a, kb * kKBlock, 0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)nb * tx_block);
+        for (int j = 0; j < nb; ++j) {
+          tma_load_2d_hint(stage_w(st, j), &tmap_w, (ks * p.bps + j) * kKBlock, row0, &full[s], pol);
+          tma_load_2d(stage_a(st, p.bps, p.b_bytes, j), &tmap_a, (ks * p.bps + j) * kKBlock, 0, &full[s]);
+        }
         ++issued;
       }
-      for (int kb = max(0, issued - p.nst); kb < issued; ++kb) {
-        if (!mbar_wait(&full[kb % p.nst], (uint32_t)(kb / p.nst) & 1u)) set_status(p.status, kStatusTimeout);
+      for (int ks = max(0, issued - p.nst); ks < issued; ++ks) {
+        if (!mbar_wait(&full[ks % p.nst], (uint32_t)(ks / p.nst) & 1u)) set_status(p.status, kStatusTimeout);
       }
     }
   } else if (warp == 1) {
@@ -229,22 +254,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              | (1u << 7) | (1u << 10)          // A, B: signed int8
                              | ((uint32_t)(p.mpad >> 3) << 17) // N
                              | ((uint32_t)(kMmaRows >> 4) << 24);  // M
-      for (int kb = 0; kb < p.nkb; ++kb) {
-        const int s = kb % p.nst;
-        if (!mbar_wait(&full[s], (uint32_t)(kb / p.nst) & 1u)) {
+      for (int ks = 0; ks < p.nks; ++ks) {
+        const int s = ks % p.nst;
+        if (!mbar_wait(&full[s], (uint32_t)(ks / p.nst) & 1u)) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        const uint64_t adesc = umma_desc_sw128(st);
-        const uint64_t bdesc = umma_desc_sw128(st + kWTileBytes);
+        const int nb = min(p.bps, p.nkb - ks * p.bps);
+        for (int j = 0; j < nb; ++j) {
+          const uint64_t adesc = umma_desc_sw128(stage_w(st, j));
+          const uint64_t bdesc = umma_desc_sw128(stage_a(st, p.bps, p.b_bytes, j));
 #pragma unroll
-        for (int kk = 0; kk < kKBlock / 32; ++kk) {
-          // advance the start address by 32 bytes (K = 32 int8) per step
-          tc_mma_i8(tmem_d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
-                    (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kKBlock / 32; ++kk) {
+            // advance the start address by 32 bytes (K = 32 int8) per step
+            tc_mma_i8(tmem_d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
+                      (ks > 0 || j > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         tc_commit(&empty[s]);
       }
@@ -354,7 +382,7 @@ struct GemmBatchParams {
   float inv_out_scale;
   int64_t ldo;
   int32_t count, m, n, k;
-  int32_t mpad, nkb, nst, stage_bytes, b_bytes, tile_rows, tma_store;
+  int32_t mpad, nkb, bps, nks, nst, stage_bytes, b_bytes, tile_rows, tma_store;
   uint32_t tmem_cols;
   uint32_t *status;
 };
@@ -386,7 +414,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * p.tile_rows;
-  const int total = p.count * p.nkb;
+  const int total = p.count * p.nks;  // stages over all GEMMs
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.nst; ++s) {
@@ -419,31 +447,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         prefetch_tmap(&maps.a[i]);
       }
       const uint64_t pol = l2_policy_evict_first();
-      const uint32_t tx = (uint32_t)(p.tile_rows * kKBlock + p.b_bytes);
+      const uint32_t tx_block = (uint32_t)(p.tile_rows * kKBlock + p.b_bytes);
       const int pre = min(p.nst, total);
       // weights of the first stages, before the previous grid has finished
       for (int gs = 0; gs < pre; ++gs) {
-        mbar_arrive_expect_tx(&full[gs], tx);
-        tma_load_2d_hint(stages + (size_t)gs * p.stage_bytes, &maps.w[gs / p.nkb], (gs % p.nkb) * kKBlock, row0,
-                         &full[gs], pol);
+        const int i = gs / p.nks, ks = gs % p.nks, nb = min(p.bps, p.nkb - ks * p.bps);
+        uint8_t *st = stages + (size_t)gs * p.stage_bytes;
+        mbar_arrive_expect_tx(&full[gs], (uint32_t)nb * tx_block);
+        for (int j = 0; j < nb; ++j)
+          tma_load_2d_hint(stage_w(st, j), &maps.w[i], (ks * p.bps + j) * kKBlock, row0, &full[gs], pol);
       }
       pdl_wait();
       pdl_trigger();
-      for (int gs = 0; gs < pre; ++gs)
-        tma_load_2d(stages + (size_t)gs * p.stage_bytes + kWTileBytes, &maps.a[gs / p.nkb], (gs % p.nkb) * kKBlock,
-                    0, &full[gs]);
+      for (int gs = 0; gs < pre; ++gs) {
+        const int i = gs / p.nks, ks = gs % p.nks, nb = min(p.bps, p.nkb - ks * p.bps);
+        uint8_t *st = stages + (size_t)gs * p.stage_bytes;
+        for (int j = 0; j < nb; ++j)
+          tma_load_2d(stage_a(st, p.bps, p.b_bytes, j), &maps.a[i], (ks * p.bps + j) * kKBlock, 0, &full[gs]);
+      }
       int issued = pre;
       for (int gs = pre; gs < total; ++gs) {
-        const int s = gs % p.nst, i = gs / p.nkb, kb = gs % p.nkb;
+        const int s = gs % p.nst, i = gs / p.nks, ks = gs % p.nks, nb = min(p.bps, p.nkb - ks * p.bps);
         if (!mbar_wait(&empty[s], (uint32_t)((gs / p.nst) - 1) & 1u)) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d_hint(st, &maps.w[i], kb * kKBlock, row0, &full[s], pol);
-        tma_load_2d(st + kWTileBytes, &maps.a[i], kb * kKBlock, 0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)nb * tx_block);
+        for (int j = 0; j < nb; ++j) {
+          tma_load_2d_hint(stage_w(st, j), &maps.w[i], (ks * p.bps + j) * kKBlock, row0, &full[s], pol);
+          tma_load_2d(stage_a(st, p.bps, p.b_bytes, j), &maps.a[i], (ks * p.bps + j) * kKBlock, 0, &full[s]);
+        }
         ++issued;
       }
       for (int gs = max(0, issued - p.nst); gs < issued; ++gs) {
@@ -469,7 +504,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_d + (uint32_t)(b * p.mpad);
-        for (int kb = 0; kb < p.nkb; ++kb, ++gs) {
+        for (int ks = 0; ks < p.nks; ++ks, ++gs) {
           const int s = gs % p.nst;
           if (!mbar_wait(&full[s], (uint32_t)(gs / p.nst) & 1u)) {
             set_status(p.status, kStatusTimeout);
@@ -479,11 +514,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           tc_fence_after();
           uint8_t *st = stages + (size_t)s * p.stage_bytes;
-          const uint64_t adesc = umma_desc_sw128(st);
-          const uint64_t bdesc = umma_desc_sw128(st + kWTileBytes);
+          const int nb = min(p.bps, p.nkb - ks * p.bps);
+          for (int j = 0; j < nb; ++j) {
+            const uint64_t adesc = umma_desc_sw128(stage_w(st, j));
+            const uint64_t bdesc = umma_desc_sw128(stage_a(st, p.bps, p.b_bytes, j));
 #pragma unroll
-          for (int kk = 0; kk < kKBlock / 32; ++kk)
-            tc_mma_i8(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kKBlock / 32; ++kk)
+              tc_mma_i8(d, adesc + (uint64_t)(kk * 2), bdesc + (uint64_t)(kk * 2), idesc,
+                        (ks > 0 || j > 0 || kk > 0) ? 1u : 0u);
+          }
           tc_commit(&empty[s]);
         }
         if (!stop) tc_commit(&acc_full[b]);  // fires once GEMM i's MMAs have completed
@@ -603,6 +642,16 @@ bool tc_shape_ok(const GemmI8Launch &a) {
 
 int gemm_i8_path(const GemmI8Launch &a) { return tc_shape_ok(a) ? 1 : 0; }
 
+namespace {
+// K blocks per stage: KS_B200_GEMM_BLOCKS (1, 2 or 4), default 4, never more than K has.
+// Measured at 14336 x 4096 (batched, M = 8): 14.8 / 10.1 / 8.8 us for 1 / 2 / 4.
+int gemm_blocks_per_stage(int nkb) {
+  static const int env = env_int("KS_B200_GEMM_BLOCKS", 4);
+  const int b = env >= 4 ? 4 : env >= 2 ? 2 : 1;
+  return std::max(1, std::min(b, nkb));
+}
+}  // namespace
+
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device) {
   GemmParams p{};
   p.sa = a.sa;
@@ -629,7 +678,7 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
   p.mpad = (int32_t)((a.m + 15) / 16 * 16);
   p.nkb = (int32_t)((a.k + kKBlock - 1) / kKBlock);
   p.b_bytes = p.mpad * kKBlock;
-  p.stage_bytes = kWTileBytes + p.b_bytes;  // multiple of 1024
+  p.bps = gemm_blocks_per_stage(p.nkb);
   uint32_t cols = 32;
   while (cols < (uint32_t)p.mpad) cols <<= 1;
   p.tmem_cols = cols;
@@ -644,9 +693,13 @@ cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int devic
   p.tile_rows = (int32_t)std::min<int64_t>(kMmaRows, (std::max(even, floor_rows) + 15) / 16 * 16);
   const int grid = (int)((a.n + p.tile_rows - 1) / p.tile_rows);
   const int reserve = 1024 /* alignment slack */ + kBarRegion + kScaleRegion;
+  // at least two stages in flight: fewer blocks per stage for many tokens
+  while (p.bps > 1 && (dp.smem_optin - reserve) / (p.bps * (kWTileBytes + p.b_bytes)) < 2) p.bps /= 2;
+  p.nks = (p.nkb + p.bps - 1) / p.bps;
+  p.stage_bytes = p.bps * (kWTileBytes + p.b_bytes);  // multiple of 1024
   int nst = (dp.smem_optin - reserve) / p.stage_bytes;
   nst = std::min(nst, std::max(1, std::min(kMaxStages, env_int("KS_B200_GEMM_STAGES", 8))));
-  nst = std::min(nst, p.nkb);
+  nst = std::min(nst, p.nks);
   if (nst < 1) return cudaErrorInvalidValue;
   p.nst = nst;
   CUtensorMap mw, ma, mo;
@@ -718,7 +771,7 @@ cudaError_t launch_gemm_i8_batch(const GemmI8Launch &shape, const GemmI8Batch &b
   p.mpad = (int32_t)((shape.m + 15) / 16 * 16);
   p.nkb = (int32_t)((shape.k + kKBlock - 1) / kKBlock);
   p.b_bytes = p.mpad * kKBlock;
-  p.stage_bytes = kWTileBytes + p.b_bytes;
+  p.bps = gemm_blocks_per_stage(p.nkb);
   uint32_t cols = 32;
   while (cols < (uint32_t)(2 * p.mpad)) cols <<= 1;
   p.tmem_cols = cols;
@@ -729,6 +782,10 @@ cudaError_t launch_gemm_i8_batch(const GemmI8Launch &shape, const GemmI8Batch &b
   p.tile_rows = (int32_t)std::min<int64_t>(kMmaRows, (std::max(even, floor_rows) + 15) / 16 * 16);
   const int grid = (int)((shape.n + p.tile_rows - 1) / p.tile_rows);
   const int reserve = 1024 /* alignment slack */ + kBatchTileBytes + kBarRegion + 2 * kBatchMaxTokens * 4;
+  // at least two stages in flight
+  while (p.bps > 1 && (dp.smem_optin - reserve) / (p.bps * (kWTileBytes + p.b_bytes)) < 2) p.bps /= 2;
+  p.nks = (p.nkb + p.bps - 1) / p.bps;
+  p.stage_bytes = p.bps * (kWTileBytes + p.b_bytes);
   int nst_cap = (dp.smem_optin - reserve) / p.stage_bytes;
   nst_cap = std::min(nst_cap, std::max(1, std::min(kMaxStages, env_int("KS_B200_GEMM_STAGES", 8))));
   if (nst_cap < 1) return cudaErrorInvalidValue;
@@ -744,7 +801,7 @@ cudaError_t launch_gemm_i8_batch(const GemmI8Launch &shape, const GemmI8Batch &b
     GemmBatchMaps maps;
     std::memset(&maps, 0, sizeof(maps));
     p.count = cnt;
-    p.nst = std::min<int>(nst_cap, cnt * p.nkb);
+    p.nst = std::min<int>(nst_cap, cnt * p.nks);
     bool tma_store = shape.ldo % 16 == 0;
     for (int j = 0; j < cnt; ++j) {
       const int i = i0 + j;
