@@ -13,19 +13,21 @@
 //
 // Swap-AB as in the INT8 GEMM: weight rows fill the MMA's M = 128 (TMEM
 // lanes), tokens its N (padded to 16).  A CTA owns `tile_rows` weight rows
-// (the same share for every SM, a multiple of 16).  Per stage of 128 K:
+// (the same share for every SM, a multiple of 16).  K streams in stages of up
+// to four 128-K blocks (one barrier round trip per stage in every hand-off;
+// each round trip costs the MMA thread a few hundred cycles).  Per block:
 //   warp 0    TMA: the packed weight tile [tile_rows x 64 B] (no swizzle),
-//             the token tile [Mpad x 128 B] (128-byte swizzle) and, every
-//             16 / (scales per stage x scale bytes) stages, a scale tile
-//             [tile_rows x 16 B] into a small ring of its own.  No multicast.
+//             the token tile [Mpad x 128 B] (128-byte swizzle) and, once per
+//             one or more stages, a scale box [tile_rows x 16..64 B] into a
+//             small ring of its own.  No multicast.
 //   warps 2-5 unpack: one weight row each, int4 -> int8 holding 16 x the
 //             weight (shift + mask per 4 bytes, PRMT to interleave), written
 //             in the UMMA K-major 128-byte-swizzle layout; proxy fence; arrive.
 //   warp 1    MMA: per group, tcgen05.mma (K = 32 each, G / 32 of them) into
 //             the group's own TMEM column block (fresh accumulate), buffered
-//             over as many stages as 512 TMEM columns hold (up to 8);
-//             commits free the stage and hand the
-//             buffer to the epilogue.
+//             over as many stages as 512 TMEM columns hold (at least 2, up
+//             to 8); one commit per stage frees it, one hands the buffer to
+//             the epilogue.
 //   warps 6-9 epilogue: tcgen05.ld each group's int32 accumulators (one TMEM
 //             lane per weight row), acc[m] += f32(v) * (s[n, g] / 16) in
 //             registers,
@@ -53,8 +55,6 @@ constexpr int kRows = 128;         // MMA M
 constexpr int kStageK = 128;       // K elements per stage: one 128-byte int8 swizzle row
 constexpr int kPacked = kStageK / 2;  // packed weight bytes per row per stage
 constexpr int kThreads = 320;      // 0 producer, 1 MMA, 2-5 unpack, 6-9 epilogue
-constexpr int kUnpackThreads = 128;
-constexpr int kScaleBox = 16;      // scale bytes per row per TMA box
 constexpr int kScaleRing = 4;
 constexpr int kMaxStagesW4 = 8;
 constexpr int kMaxBufs = 8;
@@ -65,21 +65,20 @@ struct W4GemmParams {
   int64_t ldy;
   const float *sx;
   int32_t m, n, k;
-  int32_t nkb;        // stages (K / 128, rounded up)
+  int32_t nkb;        // 128-K blocks (K / 128, rounded up)
+  int32_t bps;        // blocks per ring stage (one barrier round trip per stage in every ring)
+  int32_t nks;        // stages: nkb / bps, rounded up
   int32_t nst;        // ring stages
   int32_t tile_rows;
-  int32_t gps;        // groups per stage: 128 / G
+  int32_t gps;        // groups per block: 128 / G (at least 1)
   int32_t kpg;        // MMAs (K = 32) per group: G / 32
   int32_t sbytes;     // 2 (f16) or 4 (f32)
-  int32_t spb;        // stages per scale box: 16 / (gps * sbytes)
-  int32_t stage_bytes, a_bytes, pk_bytes, sbox_bytes;
+  int32_t sbox;       // scale bytes per row per box: max(16, bps * gps * sbytes)
+  int32_t spb;        // stages per scale box
+  int32_t stage_bytes, a_bytes, pk_bytes, sbox_bytes;  // a_bytes, pk_bytes: per block
   int32_t nbuf;       // TMEM accumulator buffers (stages the MMA may run ahead of the epilogue)
   uint32_t tmem_cols;
   uint32_t *status;
-};
-
-struct W4Smem {  // byte offsets inside the 1024-aligned dynamic shared memory
-  int32_t stages, sboxes, bars;
 };
 
 // 8 signed int4 (value 2b in the low nibble of byte b, 2b + 1 in the high
@@ -101,12 +100,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmap_s, const W4GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // [stage 0 .. nst-1: weight operand 16 KB | token tile | packed tile] [scale boxes] [barriers]
+  // [stage 0 .. nst-1: bps int8 operands (16 KB each) | bps token tiles | bps packed tiles]
+  // [scale boxes] [barriers]
   uint8_t *stages = smem;
   uint8_t *sboxes = smem + (size_t)p.nst * p.stage_bytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(sboxes + (size_t)kScaleRing * p.sbox_bytes);
   uint64_t *full = bars;                      // [nst]  TMA landed
-  uint64_t *unpacked = full + kMaxStagesW4;   // [nst]  int8 operand written
+  uint64_t *unpacked = full + kMaxStagesW4;   // [nst]  int8 operands written
   uint64_t *empty = unpacked + kMaxStagesW4;  // [nst]  MMAs of the stage done
   uint64_t *mma_done = empty + kMaxStagesW4;  // [nbuf] TMEM buffer ready
   uint64_t *tmem_free = mma_done + kMaxBufs;  // [nbuf] TMEM buffer read
@@ -117,6 +117,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * p.tile_rows;
+  const int tok_off = p.bps * kOpBytes;                  // token tiles of a stage
+  const int pk_off = p.bps * (kOpBytes + p.a_bytes);     // packed tiles of a stage
+  auto blocks_of = [&](int ks) { return min(p.bps, p.nkb - ks * p.bps); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.nst; ++s) {
@@ -145,7 +148,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
-  const int a_off = kOpBytes, pk_off = kOpBytes + p.a_bytes;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
@@ -155,35 +157,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap_s);
       pdl_wait();
       const uint64_t pol = l2_policy_evict_first();
-      const uint32_t tx = (uint32_t)(p.tile_rows * kPacked + MPAD * kStageK);
+      const uint32_t tx_block = (uint32_t)(p.tile_rows * kPacked + MPAD * kStageK);
       int issued = 0, boxes = 0;
-      for (int kb = 0; kb < p.nkb; ++kb) {
-        const int s = kb % p.nst;
-        if (kb >= p.nst && !mbar_wait(&empty[s], (uint32_t)((kb / p.nst) - 1) & 1u)) {
+      for (int ks = 0; ks < p.nks; ++ks) {
+        const int s = ks % p.nst;
+        if (ks >= p.nst && !mbar_wait(&empty[s], (uint32_t)((ks / p.nst) - 1) & 1u)) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
-        if (kb % p.spb == 0) {
-          const int bi = kb / p.spb, sb = bi % kScaleRing;
+        if (ks % p.spb == 0) {
+          const int bi = ks / p.spb, sb = bi % kScaleRing;
           if (bi >= kScaleRing && !mbar_wait(&sempty[sb], (uint32_t)((bi / kScaleRing) - 1) & 1u)) {
             set_status(p.status, kStatusTimeout);
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&sfull[sb], (uint32_t)(p.tile_rows * kScaleBox));
-          tma_load_2d(sboxes + (size_t)sb * p.sbox_bytes, &tmap_s, bi * kScaleBox, row0, &sfull[sb]);
+          mbar_arrive_expect_tx(&sfull[sb], (uint32_t)(p.tile_rows * p.sbox));
+          tma_load_2d(sboxes + (size_t)sb * p.sbox_bytes, &tmap_s, bi * p.sbox, row0, &sfull[sb]);
           ++boxes;
         }
+        const int nb = blocks_of(ks);
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], tx);
-        tma_load_2d_hint(st + pk_off, &tmap_w, kb * kPacked, row0, &full[s], pol);
-        tma_load_2d(st + a_off, &tmap_a, kb * kStageK, 0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)nb * tx_block);
+        for (int j = 0; j < nb; ++j) {
+          const int kb = ks * p.bps + j;
+          tma_load_2d_hint(st + pk_off + j * p.pk_bytes, &tmap_w, kb * kPacked, row0, &full[s], pol);
+          tma_load_2d(st + tok_off + j * p.a_bytes, &tmap_a, kb * kStageK, 0, &full[s]);
+        }
         ++issued;
       }
       pdl_trigger();
-      for (int kb = max(0, issued - p.nst); kb < issued; ++kb)
-        if (!mbar_wait(&full[kb % p.nst], (uint32_t)(kb / p.nst) & 1u)) set_status(p.status, kStatusTimeout);
+      for (int ks = max(0, issued - p.nst); ks < issued; ++ks)
+        if (!mbar_wait(&full[ks % p.nst], (uint32_t)(ks / p.nst) & 1u)) set_status(p.status, kStatusTimeout);
       for (int bi = max(0, boxes - kScaleRing); bi < boxes; ++bi)
         if (!mbar_wait(&sfull[bi % kScaleRing], (uint32_t)(bi / kScaleRing) & 1u))
           set_status(p.status, kStatusTimeout);
@@ -193,23 +199,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MPAD >> 3) << 17) |
                              ((uint32_t)(kRows >> 4) << 24);
-      for (int kb = 0; kb < p.nkb; ++kb) {
-        const int s = kb % p.nst, b = kb % p.nbuf;
-        if (!mbar_wait(&unpacked[s], (uint32_t)(kb / p.nst) & 1u) ||
-            (kb >= p.nbuf && !mbar_wait(&tmem_free[b], (uint32_t)((kb / p.nbuf) - 1) & 1u))) {
+      for (int ks = 0; ks < p.nks; ++ks) {
+        const int s = ks % p.nst, b = ks % p.nbuf;
+        if (!mbar_wait(&unpacked[s], (uint32_t)(ks / p.nst) & 1u) ||
+            (ks >= p.nbuf && !mbar_wait(&tmem_free[b], (uint32_t)((ks / p.nbuf) - 1) & 1u))) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        const uint64_t adesc = umma_desc_sw128(st);
-        const uint64_t bdesc = umma_desc_sw128(st + a_off);
-        for (int j = 0; j < p.gps; ++j) {
-          const uint32_t d = tmem_d + (uint32_t)((b * p.gps + j) * MPAD);
-          for (int kk = 0; kk < p.kpg; ++kk) {
-            const int kx = j * p.kpg + kk;  // 32-element step inside the 128-byte row
-            tc_mma_i8(d, adesc + (uint64_t)(2 * kx), bdesc + (uint64_t)(2 * kx), idesc, kk > 0 ? 1u : 0u);
+        const int nb = blocks_of(ks);
+        for (int j = 0; j < nb; ++j) {
+          const uint64_t adesc = umma_desc_sw128(st + j * kOpBytes);
+          const uint64_t bdesc = umma_desc_sw128(st + tok_off + j * p.a_bytes);
+          for (int g = 0; g < p.gps; ++g) {
+            const uint32_t d = tmem_d + (uint32_t)(((b * p.bps + j) * p.gps + g) * MPAD);
+            for (int kk = 0; kk < p.kpg; ++kk) {
+              const int kx = g * p.kpg + kk;  // 32-element step inside the 128-byte row
+              tc_mma_i8(d, adesc + (uint64_t)(2 * kx), bdesc + (uint64_t)(2 * kx), idesc, kk > 0 ? 1u : 0u);
+            }
           }
         }
         tc_commit(&empty[s]);
@@ -219,31 +228,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 6) {
     // -------------------------------------------------------------- unpack --
     const int r = threadIdx.x - 64;  // weight row of the tile
-    bool stop = false;
-    for (int kb = 0; kb < p.nkb && !stop; ++kb) {
-      const int s = kb % p.nst;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(kb / p.nst) & 1u))) {
+    for (int ks = 0; ks < p.nks; ++ks) {
+      const int s = ks % p.nst;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(ks / p.nst) & 1u))) {
         if (lane == 0) set_status(p.status, kStatusTimeout);
-        stop = true;
         break;
       }
       uint8_t *st = stages + (size_t)s * p.stage_bytes;
+      const int nb = blocks_of(ks);
       if (r < p.tile_rows) {
-        const uint8_t *src = st + pk_off + (size_t)r * kPacked;
-        uint8_t *dst = st + (size_t)r * kStageK;
+        for (int j = 0; j < nb; ++j) {
+          const uint8_t *src = st + pk_off + j * p.pk_bytes + (size_t)r * kPacked;
+          uint8_t *dst = st + j * kOpBytes + (size_t)r * kStageK;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 16 packed bytes = 32 weights = two 16-byte output chunks
-          const uint4 v = lds128(src + 16 * q);
-          uint32_t o[8];
-          unpack8x16(v.x, o[0], o[1]);
-          unpack8x16(v.y, o[2], o[3]);
-          unpack8x16(v.z, o[4], o[5]);
-          unpack8x16(v.w, o[6], o[7]);
+          for (int q = 0; q < 4; ++q) {  // 16 packed bytes = 32 weights = two 16-byte output chunks
+            const uint4 v = lds128(src + 16 * q);
+            uint32_t o[8];
+            unpack8x16(v.x, o[0], o[1]);
+            unpack8x16(v.y, o[2], o[3]);
+            unpack8x16(v.z, o[4], o[5]);
+            unpack8x16(v.w, o[6], o[7]);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int c = 2 * q + h;  // 16-byte chunk of the 128-byte row, swizzled by the row within its 8
-            *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) =
-                make_uint4(o[4 * h], o[4 * h + 1], o[4 * h + 2], o[4 * h + 3]);
+            for (int h = 0; h < 2; ++h) {
+              const int c = 2 * q + h;  // 16-byte chunk of the 128-byte row, swizzled by the row within its 8
+              *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) =
+                  make_uint4(o[4 * h], o[4 * h + 1], o[4 * h + 2], o[4 * h + 3]);
+            }
           }
         }
       }
@@ -263,25 +273,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < MPAD; ++t) acc[t] = 0.0f;
     bool stop = false;
     const uint32_t lane_base = tmem_d + ((uint32_t)(quarter * 32) << 16);
-    for (int kb = 0; kb < p.nkb && !stop; ++kb) {
-      const int b = kb % p.nbuf;
-      const int bi = kb / p.spb, sb = bi % kScaleRing;
+    const int gst = p.bps * p.gps;  // group accumulators per full stage
+    for (int ks = 0; ks < p.nks && !stop; ++ks) {
+      const int b = ks % p.nbuf;
+      const int bi = ks / p.spb, sb = bi % kScaleRing;
       bool ok = true;
-      if (kb % p.spb == 0) ok = mbar_wait(&sfull[sb], (uint32_t)(bi / kScaleRing) & 1u);
-      ok = ok && mbar_wait(&mma_done[b], (uint32_t)(kb / p.nbuf) & 1u);
+      if (ks % p.spb == 0) ok = mbar_wait(&sfull[sb], (uint32_t)(bi / kScaleRing) & 1u);
+      ok = ok && mbar_wait(&mma_done[b], (uint32_t)(ks / p.nbuf) & 1u);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) set_status(p.status, kStatusTimeout);
         stop = true;
         break;
       }
       tc_fence_after();
-      const uint8_t *srow = sboxes + (size_t)sb * p.sbox_bytes + (size_t)r * kScaleBox;
+      const uint8_t *srow = sboxes + (size_t)sb * p.sbox_bytes + (size_t)r * p.sbox;
+      const int gbase = (ks % p.spb) * gst;  // this stage's first group inside the box row
+      const int ng = blocks_of(ks) * p.gps;  // groups computed in this stage
       // The stage's group accumulators are contiguous TMEM columns
-      // ((b * gps + j) * MPAD): up to 64 of them are loaded before one wait.
+      // ((b * bps + j) * gps + g) * MPAD: up to 64 of them are loaded before one wait.
       constexpr int GPC = MPAD >= 48 ? 1 : 64 / MPAD;  // groups per load batch
-      for (int j0 = 0; j0 < p.gps; j0 += GPC) {
-        const int nvals = min(GPC, p.gps - j0) * MPAD;
-        const uint32_t col = lane_base + (uint32_t)((b * p.gps + j0) * MPAD);
+      for (int g0 = 0; g0 < ng; g0 += GPC) {
+        const int nvals = min(GPC, ng - g0) * MPAD;
+        const uint32_t col = lane_base + (uint32_t)((b * gst + g0) * MPAD);
         uint32_t v0[16], v1[16], v2[16], v3[16];
         tc_ld16_nowait(col, v0);
         if (16 < nvals) tc_ld16_nowait(col + 16u, v1);
@@ -291,14 +304,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_ld(v2, v3);  // nothing left to wait for: passes v2, v3 through the wait
         float sc[GPC];
 #pragma unroll
-        for (int jj = 0; jj < GPC; ++jj) {
+        for (int gg = 0; gg < GPC; ++gg) {
           // the box holds tile_rows rows: lanes at and above them have no weight row
-          const int gi = (kb % p.spb) * p.gps + j0 + jj;  // scale index inside the box row
-          sc[jj] = 0.0f;
-          if (r < p.tile_rows && j0 + jj < p.gps)
-            sc[jj] = p.sbytes == 2 ? __half2float(*reinterpret_cast<const __half *>(srow + 2 * gi))
+          const int gi = gbase + g0 + gg;  // scale index inside the box row
+          sc[gg] = 0.0f;
+          if (r < p.tile_rows && g0 + gg < ng)
+            sc[gg] = p.sbytes == 2 ? __half2float(*reinterpret_cast<const __half *>(srow + 2 * gi))
                                    : *reinterpret_cast<const float *>(srow + 4 * gi);
-          sc[jj] = __fmul_rn(sc[jj], 0.0625f);  // the operand holds 16 x the weights
+          sc[gg] = __fmul_rn(sc[gg], 0.0625f);  // the operand holds 16 x the weights
         }
 #pragma unroll
         for (int f = 0; f < GPC * MPAD && f < 64; ++f) {
@@ -310,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&tmem_free[b]);
-        if (kb % p.spb == p.spb - 1 || kb == p.nkb - 1) mbar_arrive(&sempty[sb]);
+        if (ks % p.spb == p.spb - 1 || ks == p.nks - 1) mbar_arrive(&sempty[sb]);
       }
     }
     if (!stop && row_ok) {
@@ -388,7 +401,6 @@ cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int d
   p.gps = (int32_t)(kStageK / a.group) > 0 ? (int32_t)(kStageK / a.group) : 1;
   p.kpg = (int32_t)(a.group / 32);
   p.sbytes = a.stype == kScaleF16 ? 2 : 4;
-  p.spb = kScaleBox / (p.gps * p.sbytes);
   const int64_t slots = dp.sm_count;
   const int64_t waves = (a.n + slots * kRows - 1) / (slots * kRows);
   const int64_t even = (a.n + waves * slots - 1) / (waves * slots);
@@ -396,22 +408,39 @@ cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int d
   const int grid = (int)((a.n + p.tile_rows - 1) / p.tile_rows);
   p.a_bytes = mpad * kStageK;  // multiple of 2048
   p.pk_bytes = (p.tile_rows * kPacked + 1023) / 1024 * 1024;
-  p.stage_bytes = kOpBytes + p.a_bytes + p.pk_bytes;
-  p.sbox_bytes = (p.tile_rows * kScaleBox + 127) / 128 * 128;
-  const int per_buf = p.gps * mpad;  // TMEM columns of one stage's group accumulators
+  // Blocks per stage: KS_B200_W4GEMM_BLOCKS (1, 2 or 4), default 4, halved
+  // until TMEM holds two stages of group accumulators and shared memory two
+  // stages (fewer barrier round trips per MMA; each costs the MMA thread a
+  // few hundred cycles).
+  static const int env_bps = env_int("KS_B200_W4GEMM_BLOCKS", 4);
+  int bps = env_bps >= 4 ? 4 : env_bps >= 2 ? 2 : 1;
+  bps = std::max(1, std::min<int>(bps, p.nkb));
+  auto sbox_of = [&](int bb) { return std::max(16, bb * p.gps * p.sbytes); };
+  auto sbox_bytes_of = [&](int bb) { return (p.tile_rows * sbox_of(bb) + 127) / 128 * 128; };
+  auto fixed_of = [&](int bb) { return 1024 /* alignment */ + kScaleRing * sbox_bytes_of(bb) + 512 /* barriers */; };
+  auto stage_of = [&](int bb) { return bb * (kOpBytes + p.a_bytes + p.pk_bytes); };
+  while (bps > 1 && (512 / (bps * p.gps * mpad) < 2 || (dp.smem_optin - fixed_of(bps)) / stage_of(bps) < 2)) bps /= 2;
+  p.bps = bps;
+  p.nks = (p.nkb + bps - 1) / bps;
+  p.sbox = sbox_of(bps);
+  p.spb = p.sbox / (bps * p.gps * p.sbytes);
+  p.sbox_bytes = sbox_bytes_of(bps);
+  p.stage_bytes = stage_of(bps);
+  const int per_buf = bps * p.gps * mpad;  // TMEM columns of one stage's group accumulators
   p.nbuf = std::min(kMaxBufs, 512 / per_buf);
   if (p.nbuf < 2) return cudaErrorNotSupported;
   uint32_t cols = 32;
   while (cols < (uint32_t)(p.nbuf * per_buf)) cols <<= 1;
   p.tmem_cols = cols;
-  const int fixed = 1024 /* alignment */ + kScaleRing * p.sbox_bytes + 512 /* barriers */;
-  int nst = std::min({kMaxStagesW4, (dp.smem_optin - fixed) / p.stage_bytes, p.nkb});
+  const int fixed = fixed_of(bps);
+  int nst = std::min({kMaxStagesW4, (dp.smem_optin - fixed) / p.stage_bytes, p.nks,
+                      std::max(1, env_int("KS_B200_W4GEMM_STAGES", kMaxStagesW4))});
   if (nst < 1) return cudaErrorNotSupported;
   p.nst = nst;
   CUtensorMap mw, ma, ms;
   if (!make_plain_map(&mw, a.w, a.n, a.k / 2, a.wstride, kPacked, p.tile_rows) ||
       !make_map(&ma, a.a, a.m, a.k, a.lda, mpad) ||
-      !make_plain_map(&ms, a.s, a.n, a.k / a.group * p.sbytes, a.sstride * p.sbytes, kScaleBox, p.tile_rows))
+      !make_plain_map(&ms, a.s, a.n, a.k / a.group * p.sbytes, a.sstride * p.sbytes, p.sbox, p.tile_rows))
     return cudaErrorInvalidValue;
   const size_t smem = (size_t)fixed + (size_t)nst * p.stage_bytes;
   switch (mpad) {
