@@ -71,7 +71,8 @@ def test_bench_shape_sampled_rows(ks, cuda, oracle, m):
 
 
 @pytest.mark.parametrize("shape", [(1, 256, 128, 128, True), (16, 1000, 4096, 64, False), (33, 500, 11008, 32, True),
-                                   (64, 384, 2048, 32, False), (5, 130, 512, 128, False), (48, 208, 4096, 64, True)])
+                                   (64, 384, 2048, 32, False), (5, 130, 512, 128, False), (48, 208, 4096, 64, True),
+                                   (8, 300, 384, 32, True), (8, 300, 640, 64, True), (12, 96, 1152, 128, False)])
 def test_shapes_all_rows(ks, cuda, oracle, shape):
     import torch
 

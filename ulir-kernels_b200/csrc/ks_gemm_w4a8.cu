@@ -414,7 +414,9 @@ cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int d
   // few hundred cycles).
   static const int env_bps = env_int("KS_B200_W4GEMM_BLOCKS", 4);
   int bps = env_bps >= 4 ? 4 : env_bps >= 2 ? 2 : 1;
-  bps = std::max(1, std::min<int>(bps, p.nkb));
+  // a power of two, so the scale bytes per stage are too (TMA boxes and their
+  // x coordinates must be multiples of 16 bytes)
+  while (bps > p.nkb) bps /= 2;
   auto sbox_of = [&](int bb) { return std::max(16, bb * p.gps * p.sbytes); };
   auto sbox_bytes_of = [&](int bb) { return (p.tile_rows * sbox_of(bb) + 127) / 128 * 128; };
   auto fixed_of = [&](int bb) { return 1024 /* alignment */ + kScaleRing * sbox_bytes_of(bb) + 512 /* barriers */; };
