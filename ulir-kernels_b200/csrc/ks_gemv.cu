@@ -366,15 +366,31 @@ bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int
   static const int ahead_single = env_int("KS_B200_L2_AHEAD_SINGLE", -1);
   static const int ahead_batch = env_int("KS_B200_L2_AHEAD_BATCH", -1);
   static const int rps_cap_batch = std::max(2, env_int("KS_B200_BATCH_ROWS_PER_STAGE", 24));
+  static const int min_batch_env = env_int("KS_B200_BATCH_MIN_STAGES", -1);
   const int smem_cta = batch ? kSmemBatch : kSmemSingle;
-  const int min_stages = batch ? 4 : min_single;
   const int row_total = row_bytes + srow_bytes;
   const int budget = smem_cta - kBarBytes - 2 * xbuf_bytes;
   if (budget <= 0) return false;
   const int64_t n_cta = std::min<int64_t>(rows, sm_count);
   const int64_t rows_cta_max = (rows + n_cta - 1) / n_cta;
-  int rps = (budget / min_stages) / row_total;
-  rps = std::min(rps, batch ? rps_cap_batch : 2 * cw);
+  int rps;
+  const int64_t half = budget / 2;
+  const int64_t bytes_cta = rows_cta_max * (int64_t)row_total;  // one matrix, one CTA
+  if (batch && min_batch_env < 0 && bytes_cta <= 2 * half) {
+    // A short stream per matrix: one or two stages of equal size per matrix,
+    // as large as two fit in the ring.  Every stage is a producer / consumer
+    // barrier round trip, and a small last stage of a matrix would cost one
+    // for few bytes (measured on B200: 11008 x 4096 W4A8, 75 rows per CTA,
+    // 4.36 us per GEMV with four stages of 22 rows, 3.99 with two of 38).
+    const int64_t per_matrix = (bytes_cta + half - 1) / half;  // 1 or 2
+    rps = (int)((rows_cta_max + per_matrix - 1) / per_matrix);
+    rps = (rps + 1) & ~1;
+  } else {
+    // A long stream per matrix (or the single-GEMV kernel): a deeper ring.
+    const int min_stages = batch ? std::max(2, min_batch_env > 0 ? min_batch_env : 4) : min_single;
+    rps = (budget / min_stages) / row_total;
+    rps = std::min(rps, batch ? rps_cap_batch : 2 * cw);
+  }
   rps = (int)std::min<int64_t>(rps, (rows_cta_max + 1) & ~int64_t(1));
   rps &= ~1;
   if (rps < 2) rps = 2;
