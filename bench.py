@@ -129,54 +129,224 @@ def make_host_inputs(seed=SEED):
     return x, w, s16
 
 
-def cpu_reference_runner():
-    """(run_one_gemv, kind, threads): the reference C on row slices across threads."""
+REF_BUILDS = ("generic", "avx2")  # the reference's generic and x86_avx2 profiles, compiled by oracle/Makefile
+
+
+class RowSlicedCPU:
+    """The reference's C on contiguous row slices across host threads (legal:
+    its functions are reentrant, include/kernelsmith/ks_quantized.h:12, and
+    rows are independent, so the result is bit-identical to one call)."""
+
+    def __init__(self, threads=None):
+        self.threads = threads or host_threads()
+        self.pool = cf.ThreadPoolExecutor(max_workers=self.threads)
+
+    def run(self, rows, call):
+        T = min(self.threads, rows)
+        bounds = [(rows * i // T, rows * (i + 1) // T - rows * i // T) for i in range(T)]
+        rcs = list(self.pool.map(lambda ab: call(*ab), bounds))
+        assert all(rc == 0 for rc in rcs), rcs
+
+    def seconds(self, fn, reps):
+        fn()  # warm-up
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    def close(self):
+        self.pool.shutdown()
+
+
+def ref_libs():
+    """{build: ctypes lib} of the reference builds present (else the oracle port as 'port')."""
     import oracle as O
 
+    libs = {b: O.RefLib(b).lib for b in REF_BUILDS if O.ref_available(b)}
+    return libs
+
+
+def w4a8_rows_call(lib, x, w, s32, y, cols, group, sx=SX):
+    """call(r0, n): the reference ks_matvec_w4a8 on rows [r0, r0 + n)."""
+    fn = lib.ks_matvec_w4a8
+    return lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
+                            s32.ctypes.data + r0 * s32.strides[0], s32.shape[1], y.ctypes.data + 4 * r0, n, cols,
+                            group, sx, 0, 0, None, 0)
+
+
+def i8_rows_call(lib, x, w, y, cols):
+    """call(r0, n): the reference ks_matvec_i8 on rows [r0, r0 + n)."""
+    fn = lib.ks_matvec_i8
+    return lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
+                            y.ctypes.data + 4 * r0, n, cols, 0, 0, None, 0)
+
+
+def port_w4a8_rows_call(x, w, s32, y, cols, group, sx=SX):
+    """The oracle port (only when the reference builds are absent)."""
+    import oracle as O
+
+    fn = O.Oracle().lib.kso_matvec_w4a8
+    return lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
+                            s32.ctypes.data + r0 * s32.strides[0], s32.shape[1], y.ctypes.data + 4 * r0, n, cols,
+                            group, sx, 0, 0)
+
+
+def w4a8_host_matrix(seed, rows, cols, group):
+    import oracle as O
+
+    x = O.rng(seed, 0).integers(-127, 128, cols, dtype=np.int8)
+    w = O.rng(seed, 1).integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    s16 = O.rng(seed, 2).uniform(1e-3, 1e-2, (rows, cols // group)).astype(np.float16)
+    return x, w, s16
+
+
+def cpu_reference_runner(build=None):
+    """(run_one_gemv, kind, threads, runner, build) for the headline GEMV:
+    the reference ks_matvec_w4a8 (f32 scales widened from the f16 set) on row
+    slices across all host threads."""
     x, w, s16 = make_host_inputs()
     s32 = s16.astype(np.float32)
     y = np.zeros(ROWS, np.float32)
-    if O.ref_available("generic"):
-        impl, kind = O.RefLib("generic"), "reference"
-        fn = impl.lib.ks_matvec_w4a8
-        call = lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
-                                s32.ctypes.data + r0 * s32.strides[0], s32.shape[1], y.ctypes.data + 4 * r0,
-                                n, COLS, GROUP, SX, 0, 0, None, 0)
+    libs = ref_libs()
+    cpu = RowSlicedCPU()
+    if libs:
+        build = build if build in libs else ("avx2" if "avx2" in libs else next(iter(libs)))
+        call, kind = w4a8_rows_call(libs[build], x, w, s32, y, COLS, GROUP), "reference"
     else:
-        impl, kind = O.Oracle(), "port"
-        fn = impl.lib.kso_matvec_w4a8
-        call = lambda r0, n: fn(x.ctypes.data, w.ctypes.data + r0 * w.strides[0], w.strides[0],  # noqa: E731
-                                s32.ctypes.data + r0 * s32.strides[0], s32.shape[1], y.ctypes.data + 4 * r0,
-                                n, COLS, GROUP, SX, 0, 0)
-    T = host_threads()
-    bounds = [(ROWS * i // T, ROWS * (i + 1) // T) for i in range(T)]
-    bounds = [(a, b - a) for a, b in bounds if b > a]
-    pool = cf.ThreadPoolExecutor(max_workers=len(bounds))
-
-    def one():
-        rcs = list(pool.map(lambda ab: call(*ab), bounds))
-        assert all(rc == 0 for rc in rcs), rcs
-
-    return one, kind, len(bounds), pool
+        build, call, kind = "oracle port", port_w4a8_rows_call(x, w, s32, y, COLS, GROUP), "port"
+    return (lambda: cpu.run(ROWS, call)), kind, cpu.threads, cpu, build
 
 
-def time_cpu_reference(n_gemvs: int, warmup: int = 1):
-    one, kind, threads, pool = cpu_reference_runner()
-    for _ in range(warmup):
-        one()
-    t0 = time.perf_counter()
-    for _ in range(n_gemvs):
-        one()
-    dt = time.perf_counter() - t0
-    pool.shutdown()
-    return dt, kind, threads
+def cpu_baseline_headline():
+    """The headline configuration on every reference build present; the
+    faster build is the line's value, the others are listed beside it."""
+    libs = ref_libs() or {"oracle port": None}
+    per_build = {}
+    for b in libs:
+        one, kind, threads, cpu, build = cpu_reference_runner(b if b in REF_BUILDS else None)
+        reps = 16
+        dt = cpu.seconds(one, reps)
+        cpu.close()
+        per_build[build] = {"us_per_gemv": dt * 1e6, "TB_s": gemv_bytes() / dt / 1e12, "kind": kind}
+    best = max(per_build, key=lambda b: per_build[b]["TB_s"])
+    return {"value": per_build[best]["TB_s"], "unit": "TB/s", "cores": host_threads(),
+            "kind": per_build[best]["kind"], "build": best, "builds": per_build,
+            "sample": f"16 GEMVs {ROWS}x{COLS} G{GROUP} per build (f32 scales widened from the f16 set), "
+                      f"rows split over {host_threads()} threads"}
+
+
+def attach_cpu_baselines(i8, gemm, layer, cfg5):
+    """Beside each secondary configuration: the reference's own C for that
+    configuration on this host's cores (both builds), rows split over all
+    threads.  The f32 / int8 epilogues (a few multiplies per output) and the
+    decode layer's RMSNorm / SiLU / quantisation are not timed; the GEMV work
+    that dominates them is."""
+    libs = ref_libs()
+    if not libs:
+        return
+    import oracle as O
+
+    peak, _ = measured_hbm_peak()
+    cpu = RowSlicedCPU()
+    T = cpu.threads
+    try:
+        if i8 is not None:  # configuration 1: ks_matvec_i8 4096 x 4096
+            x = O.rng(SEED + 31, 0).integers(-127, 128, I8_K, dtype=np.int8)
+            w = O.rng(SEED + 31, 1).integers(-127, 128, (I8_N, I8_K), dtype=np.int8)
+            y = np.zeros(I8_N, np.int32)
+            b = I8_N * I8_K + I8_K + 8 * I8_N
+            builds = {}
+            for name, lib in libs.items():
+                call = i8_rows_call(lib, x, w, y, I8_K)
+                dt = cpu.seconds(lambda: cpu.run(I8_N, call), 64)
+                builds[name] = {"us_per_gemv": dt * 1e6, "TB_s": b / dt / 1e12}
+            best = max(builds, key=lambda k: builds[k]["TB_s"])
+            i8["cpu_baseline"] = {"value": builds[best]["TB_s"], "unit": "TB/s", "cores": T, "kind": "reference",
+                                  "build": best, "builds": builds,
+                                  "sample": f"64 x ks_matvec_i8 {I8_N}x{I8_K} per build (int32 accumulate; the "
+                                            f"per-channel f32 epilogue not timed), rows over {T} threads"}
+        if gemm is not None:  # configuration 3: per token, ks_matvec_i8 over W [14336, 4096]
+            N, Kd = 14336, 4096
+            w = O.rng(SEED + 47, 1).integers(-127, 128, (N, Kd), dtype=np.int8)
+            y = np.zeros(N, np.int32)
+            res = {}
+            for M in (8, 16, 32, 64):
+                A = O.rng(SEED + 47, 2 + M).integers(-127, 128, (M, Kd), dtype=np.int8)
+                b = N * Kd + M * Kd + M * N + 4 * (M + N)
+                builds = {}
+                for name, lib in libs.items():
+                    calls = [i8_rows_call(lib, A[m], w, y, Kd) for m in range(M)]
+
+                    def one_gemm():
+                        for c in calls:
+                            cpu.run(N, c)
+
+                    dt = cpu.seconds(one_gemm, 1)
+                    builds[name] = {"us": dt * 1e6, "TB_s": b / dt / 1e12}
+                best = max(builds, key=lambda k: builds[k]["TB_s"])
+                res[f"M{M}"] = {"value": builds[best]["TB_s"], "build": best, "builds": builds}
+            gemm["cpu_baseline"] = {"unit": "TB/s", "cores": T, "kind": "reference", "per_m": res,
+                                    "sample": "one M x 4096 x 14336 GEMM per M and build as M calls of the "
+                                              "reference ks_matvec_i8 (int32 rows per token; the requantising "
+                                              f"epilogue not timed), rows over {T} threads"}
+        if layer is not None:  # configuration 4: the five W4A8 GEMVs of a layer
+            h, i = LAYER_H, LAYER_I
+            shapes = [(3 * h, h), (h, h), (i, h), (i, h), (h, i)]
+            mats = []
+            for k, (r, c) in enumerate(shapes):
+                x, w, s16 = w4a8_host_matrix(SEED + 400 + k, r, c, GROUP)
+                mats.append((r, c, x, w, s16.astype(np.float32), np.zeros(r, np.float32)))
+            builds = {}
+            for name, lib in libs.items():
+                calls = [(r, w4a8_rows_call(lib, x, w, s, y, c, GROUP)) for r, c, x, w, s, y in mats]
+
+                def one_layer():
+                    for r, call in calls:
+                        cpu.run(r, call)
+
+                dt = cpu.seconds(one_layer, 1)
+                builds[name] = {"us_per_layer": dt * 1e6, "GB_s": layer_bytes() / dt / 1e9}
+            best = max(builds, key=lambda k: builds[k]["GB_s"])
+            layer["cpu_baseline"] = {"value": builds[best]["GB_s"] / 1e3, "unit": "TB/s", "cores": T,
+                                     "kind": "reference", "build": best, "builds": builds,
+                                     "sample": "one layer = the five W4A8 GEMVs (QKV, O, gate, up, down; G32, f32 "
+                                               "scales) through the reference ks_matvec_w4a8; RMSNorm, SiLU, "
+                                               f"residuals and quantisation not timed; rows over {T} threads"}
+        if cfg5 is not None:  # configuration 5: the two large shapes
+            res = {}
+            for name, rows, _ in CFG5_SHAPES:
+                sample_rows = min(rows, 32064)  # a bounded sample of the LM head's rows
+                x, w, s16 = w4a8_host_matrix(SEED + 500 + rows, sample_rows, CFG5_COLS, CFG5_GROUP)
+                s = s16.astype(np.float32)
+                y = np.zeros(sample_rows, np.float32)
+                builds = {}
+                for bname, lib in libs.items():
+                    call = w4a8_rows_call(lib, x, w, s, y, CFG5_COLS, CFG5_GROUP)
+                    dt = cpu.seconds(lambda: cpu.run(sample_rows, call), 1)
+                    dt_full = dt * rows / sample_rows
+                    builds[bname] = {"us_per_gemv": dt_full * 1e6, "TB_s": cfg5_bytes(rows) / dt_full / 1e12}
+                best = max(builds, key=lambda k: builds[k]["TB_s"])
+                res[name] = {"value": builds[best]["TB_s"], "build": best, "builds": builds,
+                             "rows_timed": sample_rows}
+            cfg5["cpu_baseline"] = {"unit": "TB/s", "cores": T, "kind": "reference", "per_shape": res,
+                                    "sample": "one GEMV per shape and build through the reference ks_matvec_w4a8 "
+                                              "(f32 scales), the LM head on its first 32064 rows and scaled by "
+                                              f"rows; rows over {T} threads"}
+    finally:
+        cpu.close()
 
 
 def run_reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    one, kind, threads, pool = cpu_reference_runner()
+    # the faster of the reference's builds on this host (two GEMVs each)
+    probe = {}
+    for b in ref_libs() or [None]:
+        one, kind, threads, cpu, build = cpu_reference_runner(b)
+        probe[build] = cpu.seconds(one, 2)
+        cpu.close()
+    one, kind, threads, cpu, build = cpu_reference_runner(min(probe, key=probe.get))
     for _ in range(args.warmup):
         one()
     times = []
@@ -184,17 +354,19 @@ def run_reference_arm(args):
         t0 = time.perf_counter()
         one()
         times.append(time.perf_counter() - t0)
-    pool.shutdown()
+    cpu.close()
     total = sum(times)
     value = gemv_bytes() * args.steps / total / 1e12
     sample = (f"1 GEMV {ROWS}x{COLS} G{GROUP} per step (f32 scales widened from the f16 set), rows split over "
-              f"{threads} threads, reference ks_matvec_w4a8 ({'oracle/_ref generic -O3' if kind == 'reference' else 'oracle port'})")
+              f"{threads} threads, reference ks_matvec_w4a8 "
+              f"({'oracle/_ref ' + build + ' build, -O3' if kind == 'reference' else 'oracle port'})")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a8-f32acc",
         "data": "synthetic (seeded)", "config": workload_config(world),
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": kind, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": kind, "build": build,
+                         "sample": sample},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), file=_JSON_OUT, flush=True)
@@ -306,12 +478,19 @@ def run_b200_arm(args):
         raise SystemExit(f"--gemvs-per-launch must divide {MATS}")
     CHUNKS = MATS // per_launch
 
+    # NVML sampling runs from before the warm-up to the end of the run, so the
+    # line's clock record covers the GPU under load, not one sample
+    clocks = ClockSampler(dev)
+    clocks.__enter__()
     # ---- resident inputs: 64 shards of [ROWS, COLS] (this rank's rows) ----
     gen = torch.Generator(device=dev)
     gen.manual_seed(SEED + 7919 * rank)
     W = torch.randint(0, 256, (MATS, ROWS, COLS // 2), dtype=torch.uint8, device=dev, generator=gen)
     S = (torch.rand((MATS, ROWS, COLS // GROUP), device=dev, generator=gen) * 9e-3 + 1e-3).to(torch.float16)
-    X = torch.randint(-127, 128, (MATS, COLS), dtype=torch.int8, device=dev, generator=gen)
+    # x is replicated: the same activation vectors on every rank
+    genx = torch.Generator(device=dev)
+    genx.manual_seed(SEED + 1)
+    X = torch.randint(-127, 128, (MATS, COLS), dtype=torch.int8, device=dev, generator=genx)
     Yfull = torch.zeros((CHUNKS, world, MATS // CHUNKS, ROWS), dtype=torch.float32, device=dev)
     Yloc = torch.zeros((CHUNKS, MATS // CHUNKS, ROWS), dtype=torch.float32, device=dev)
     status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
@@ -328,7 +507,7 @@ def run_b200_arm(args):
     if peer:
         from kernelsmith_b200.sharded import PeerGatherW4A8
 
-        pgw = PeerGatherW4A8(MATS, ROWS, dev)
+        pgw = PeerGatherW4A8(MATS, ROWS, dev, timeout_ns=5_000_000_000)
     signals = [0] * CHUNKS
 
     def gemv_chunk(c):
@@ -385,23 +564,18 @@ def run_b200_arm(args):
         for _ in range(max(3, args.warmup)):
             step()
     torch.cuda.synchronize()
-    # NVML set-up and the sampling thread start before the ranks line up, so
-    # no rank enters the timed region late
-    clocks = ClockSampler(dev)
-    clocks.__enter__()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    try:
-        with torch.cuda.stream(main):
-            start.record(main)
-            for _ in range(args.steps):
-                step()
-            end.record(main)
-            end.synchronize()
-    finally:
-        clocks.__exit__(None, None, None)
+    n_before = len(clocks.samples)
+    with torch.cuda.stream(main):
+        start.record(main)
+        for _ in range(args.steps):
+            step()
+        end.record(main)
+        end.synchronize()
+    n_timed = len(clocks.samples) - n_before
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     rank_ms = [ms]
@@ -417,6 +591,32 @@ def run_b200_arm(args):
     if peer:
         pst = pgw.status.cpu().tolist()
         assert pst == [0, 0], f"peer-gather status {pst}"
+    gathered_check = None
+    if world > 1:
+        # values, not only status words: the gathered outputs of the first and
+        # last matrix of the last step against the single-GPU result of the
+        # full matrix on this GPU (its row blocks all-gathered from the ranks)
+        def full_out(m):
+            if peer:
+                return pgw.y[m]
+            return Yfull[m // per_chunk][:, m % per_chunk, :].reshape(-1)
+
+        ok = True
+        for m in (0, MATS - 1):
+            wf = torch.empty((world * ROWS, COLS // 2), dtype=torch.uint8, device=dev)
+            sf = torch.empty((world * ROWS, COLS // GROUP), dtype=torch.float16, device=dev)
+            dist.all_gather_into_tensor(wf, W[m].contiguous())
+            dist.all_gather_into_tensor(sf, S[m].contiguous())
+            y1 = torch.zeros(world * ROWS, dtype=torch.float32, device=dev)
+            K.matvec_w4a8_async(X[m], wf, COLS // 2, sf, COLS // GROUP, y1, world * ROWS, COLS, GROUP, SX,
+                                scale_type=K.SCALE_F16, status=status)
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(y1, full_out(m)))
+            del wf, sf
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        gathered_check = {"matrices": [0, MATS - 1], "bitwise_equal_single_gpu_on_every_rank": bool(flag.item()),
+                          "reference": "full matrix on one GPU (row blocks all-gathered), same kernel family"}
 
     # secondary: the single-GEMV launch chain (what a dependent decode chain of
     # ks_* calls costs per GEMV), timed the same way on this rank
@@ -449,21 +649,6 @@ def run_b200_arm(args):
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(1, min(args.steps, 5))
     e2e = run_e2e(L, K, torch, dist, dev, world, rank, e2e_steps) if e2e_steps > 0 else None
 
-    layer = run_decode_layers(K, torch, dev, args) if args.decode_layers > 0 else None
-    # the other configurations, single GPU only (per-GPU numbers)
-    i8 = run_int8_gemv(K, torch, dev) if world == 1 and not args.no_secondary else None
-    gemm = run_gemm(K, torch, dev) if world == 1 and not args.no_secondary else None
-    imp = run_import(K, torch, dev) if world == 1 and not args.no_secondary else None
-    gw4 = run_gemm_w4a8(K, torch, dev) if world == 1 and not args.no_secondary else None
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        n = MATS
-        dt, kind, threads = time_cpu_reference(n)
-        cpu = {"value": gemv_bytes() * n / dt / 1e12, "unit": "TB/s", "cores": threads, "kind": kind,
-               "sample": f"{n} GEMVs {ROWS}x{COLS} G{GROUP} (one step), f32 scales, rows split over {threads} "
-                         f"threads, {dt:.2f} s wall"}
-
     for g in graphs:
         del g
     graphs.clear()
@@ -472,6 +657,24 @@ def run_b200_arm(args):
         dist.barrier()
         torch.cuda.synchronize()
         pgw.close()
+    del W, S, Yfull, Yloc
+    torch.cuda.empty_cache()
+
+    # the sharded large-matrix configuration, at every N (strong scaling)
+    cfg5 = run_sharded_cfg5(K, torch, dist, dev, world, rank) if not args.no_secondary else None
+    layer = run_decode_layers(K, torch, dev, args) if args.decode_layers > 0 else None
+    # the other configurations, single GPU only (per-GPU numbers)
+    i8 = run_int8_gemv(K, torch, dev) if world == 1 and not args.no_secondary else None
+    gemm = run_gemm(K, torch, dev) if world == 1 and not args.no_secondary else None
+    imp = run_import(K, torch, dev) if world == 1 and not args.no_secondary else None
+    gw4 = run_gemm_w4a8(K, torch, dev) if world == 1 and not args.no_secondary else None
+    clocks.__exit__(None, None, None)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_headline()
+        attach_cpu_baselines(i8, gemm, layer, cfg5)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
@@ -489,6 +692,8 @@ def run_b200_arm(args):
             "single_launch_chain": {"us_per_gemv": chain_us, "GB_s": gemv_bytes() / chain_us / 1e3,
                                     "frac": gemv_bytes() / chain_us / 1e3 / peak,
                                     "note": "64 single-GEMV launches, PDL chain, per GPU"},
+            "gathered_check": gathered_check,
+            "sharded_cfg5": cfg5,
             "decode_layer": layer,
             "int8_gemv": i8,
             "gemm_i8": gemm,
@@ -497,12 +702,17 @@ def run_b200_arm(args):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": CHUNKS * args.steps * world,
-            "clocks": clocks.summary(),
+            "clocks": dict(clocks.summary(), samples_in_timed_region=n_timed,
+                           window="from before the warm-up to the end of the secondary measurements"),
         }
         print(json.dumps(line), file=_JSON_OUT, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if gathered_check is not None and not gathered_check["bitwise_equal_single_gpu_on_every_rank"]:
+        raise SystemExit("gathered outputs differ from the single-GPU result")
+    if cfg5 is not None and cfg5.get("gathered_equal_single_gpu") is False:
+        raise SystemExit("sharded configuration: gathered outputs differ from the single-GPU result")
     return 0
 
 
@@ -576,8 +786,9 @@ def run_decode_layers(K, torch, dev, args):
             "shape": "hidden 4096, inter 11008, W4A8 G32 f16 scales, batch 1, fused RMSNorm/quantise/SiLU/residual"}
 
 
-def _graph_us(torch, stream, fn, units, reps=10):
-    """Device time per unit of `fn` (graph-captured, CUDA events on `stream`)."""
+def _graph_us(torch, stream, fn, units, reps=10, before_timing=None):
+    """Device time per unit of `fn` (graph-captured, CUDA events on `stream`).
+    before_timing() runs after the warm-up replays (a barrier across ranks)."""
     with torch.cuda.stream(stream):
         fn()
     stream.synchronize()
@@ -587,6 +798,9 @@ def _graph_us(torch, stream, fn, units, reps=10):
     with torch.cuda.stream(stream):
         for _ in range(3):
             g.replay()
+        if before_timing is not None:
+            stream.synchronize()
+            before_timing()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(reps):
@@ -596,6 +810,178 @@ def _graph_us(torch, stream, fn, units, reps=10):
     us = e0.elapsed_time(e1) * 1e3 / (reps * units)
     del g
     return us
+
+
+CFG5_COLS, CFG5_GROUP = 8192, 128
+# (name, rows, distinct matrices per step): 16 x 121 MB and 4 x 542 MB of
+# weights per step on one GPU, both above the 126 MB L2 at every N
+CFG5_SHAPES = [("up_28672x8192", 28672, 16), ("lm_head_128256x8192", 128256, 4)]
+
+
+def cfg5_bytes(rows, cols=CFG5_COLS, group=CFG5_GROUP):
+    """Algorithmic bytes of one sharded-configuration GEMV over `rows` rows."""
+    return rows * (cols // 2) + rows * (cols // group) * 2 + cols + rows * 4
+
+
+def _reduce(torch, dist, dev, world, v, op):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=op)
+    return float(t.item())
+
+
+def run_sharded_cfg5(K, torch, dist, dev, world, rank, reps=10):
+    """W4A8 K=8192, N=28672 and N=128256, G128, f16 scales, split along N over
+    the ranks (strong scaling: the matrices are the same at every N).  Per GEMV,
+    max over ranks, CUDA events:
+      t_gemv   this rank's row block only, local outputs (one batched launch
+               of the step's matrices);
+      t_peer   the same launch with the gather fused into it (peer stores,
+               arrival wait);
+      t_nccl   the same launch with local outputs, then an NCCL all-gather
+               of the step's output slices (serialised after it);
+      t_peer_chain  one matrix per launch, each followed by its arrival wait
+               (a dependent chain: the next GEMV may use the gathered output);
+      t1, t1_chain  the full matrices on one GPU (measured on every rank,
+               the fastest taken), batched and one launch per matrix.
+    Efficiency(P) = t1 / (P * t(P)) for each.  After the timing every rank
+    compares the gathered outputs of two matrices bitwise with its own
+    single-GPU result."""
+    from kernelsmith_b200.sharded import NcclGatherW4A8, PeerGatherW4A8
+
+    peak, _ = measured_hbm_peak()
+    main = torch.cuda.Stream(device=dev)
+    out = {"cols": CFG5_COLS, "group": CFG5_GROUP, "scale_dtype": "f16", "n_gpus": world, "shapes": {},
+           "method": "per GEMV, CUDA events on the launching stream, max over ranks (t1: fastest rank)"}
+    all_equal = True
+    for si, (name, rows, C) in enumerate(CFG5_SHAPES):
+        R = rows // world
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(SEED + 101 * (si + 1) + 7919 * rank)
+        W = torch.randint(0, 256, (C, R, CFG5_COLS // 2), dtype=torch.uint8, device=dev, generator=gen)
+        S = (torch.rand((C, R, CFG5_COLS // CFG5_GROUP), device=dev, generator=gen) * 9e-3 + 1e-3).to(torch.float16)
+        genx = torch.Generator(device=dev)
+        genx.manual_seed(SEED + 202 * (si + 1))
+        X = torch.randint(-127, 128, (C, CFG5_COLS), dtype=torch.int8, device=dev, generator=genx)
+        Yl = torch.zeros((C, R), dtype=torch.float32, device=dev)
+        status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
+        main.wait_stream(torch.cuda.current_stream(dev))
+        xs, ws, ss = [X[m] for m in range(C)], [W[m] for m in range(C)], [S[m] for m in range(C)]
+        wst, sst = CFG5_COLS // 2, CFG5_COLS // CFG5_GROUP
+
+        def local():
+            K.matvec_w4a8_batch_async(xs, ws, ss, [Yl[m] for m in range(C)], wst, sst, R, CFG5_COLS, CFG5_GROUP, SX,
+                                      scale_type=K.SCALE_F16, status=status, stream=main)
+
+        rec = {"rows": rows, "rows_per_rank": R, "matrices_per_step": C,
+               "bytes_per_gemv_full": cfg5_bytes(rows), "bytes_per_gemv_per_rank": cfg5_bytes(R)}
+        line_up = dist.barrier if world > 1 else None
+        t_gemv = _reduce(torch, dist, dev, world, _graph_us(torch, main, local, C, reps, line_up),
+                         dist.ReduceOp.MAX)
+        rec["t_gemv_us"] = t_gemv
+        rec["gemv_frac_per_rank"] = cfg5_bytes(R) / t_gemv / 1e3 / peak
+        peer_out = nccl_out = None
+        if world > 1:
+            pg = PeerGatherW4A8(C, R, dev, timeout_ns=5_000_000_000)
+            rec["t_peer_us"] = _reduce(torch, dist, dev, world, _graph_us(
+                torch, main, lambda: pg.run(xs, ws, ss, CFG5_COLS, CFG5_GROUP, SX, K.SCALE_F16, stream=main), C,
+                reps, line_up), dist.ReduceOp.MAX)
+
+            def chain():
+                for m in range(C):
+                    pg.run([xs[m]], [ws[m]], [ss[m]], CFG5_COLS, CFG5_GROUP, SX, K.SCALE_F16, stream=main, m0=m)
+
+            rec["t_peer_chain_us"] = _reduce(torch, dist, dev, world, _graph_us(torch, main, chain, C, reps, line_up),
+                                             dist.ReduceOp.MAX)
+            # NCCL: the launch is graph-captured, the all-gather issued after each replay
+            ng = NcclGatherW4A8(C, R, dev)
+
+            def nccl_launch():
+                K.matvec_w4a8_batch_async(xs, ws, ss, [ng.y_local[m] for m in range(C)], wst, sst, R, CFG5_COLS,
+                                          CFG5_GROUP, SX, scale_type=K.SCALE_F16, status=status, stream=main)
+
+            with torch.cuda.stream(main):
+                nccl_launch()
+            main.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=main):
+                nccl_launch()
+
+            def nccl_step():
+                g.replay()
+                dist.all_gather_into_tensor(ng.y_all, ng.y_local)
+
+            with torch.cuda.stream(main):
+                for _ in range(3):
+                    nccl_step()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(main):
+                e0.record(main)
+                for _ in range(reps):
+                    nccl_step()
+                e1.record(main)
+                e1.synchronize()
+            rec["t_nccl_us"] = _reduce(torch, dist, dev, world, e0.elapsed_time(e1) * 1e3 / (reps * C),
+                                       dist.ReduceOp.MAX)
+            del g
+            peer_out, nccl_out = pg, ng
+        # single GPU: the full matrices, row blocks all-gathered from the ranks
+        if world > 1:
+            Wf = torch.empty((C, rows, CFG5_COLS // 2), dtype=torch.uint8, device=dev)
+            Sf = torch.empty((C, rows, CFG5_COLS // CFG5_GROUP), dtype=torch.float16, device=dev)
+            for m in range(C):
+                dist.all_gather_into_tensor(Wf[m], W[m])
+                dist.all_gather_into_tensor(Sf[m], S[m])
+        else:
+            Wf, Sf = W, S
+        Y1 = torch.zeros((C, rows), dtype=torch.float32, device=dev)
+
+        def full_batched():
+            K.matvec_w4a8_batch_async(xs, [Wf[m] for m in range(C)], [Sf[m] for m in range(C)],
+                                      [Y1[m] for m in range(C)], wst, sst, rows, CFG5_COLS, CFG5_GROUP, SX,
+                                      scale_type=K.SCALE_F16, status=status, stream=main)
+
+        def full_chain():
+            for m in range(C):
+                K.matvec_w4a8_async(xs[m], Wf[m], wst, Sf[m], sst, Y1[m], rows, CFG5_COLS, CFG5_GROUP, SX,
+                                    scale_type=K.SCALE_F16, status=status, stream=main)
+
+        main.wait_stream(torch.cuda.current_stream(dev))
+        t1 = _reduce(torch, dist, dev, world, _graph_us(torch, main, full_batched, C, reps), dist.ReduceOp.MIN)
+        t1c = _reduce(torch, dist, dev, world, _graph_us(torch, main, full_chain, C, reps), dist.ReduceOp.MIN)
+        full_batched()  # Y1 for the value check
+        main.synchronize()
+        rec["t1_us"], rec["t1_chain_us"] = t1, t1c
+        rec["t1_frac"] = cfg5_bytes(rows) / t1 / 1e3 / peak
+        rec["efficiency_gemv_only"] = t1 / (world * t_gemv)
+        if world > 1:
+            rec["efficiency_gemv_peer_gather"] = t1 / (world * rec["t_peer_us"])
+            rec["efficiency_gemv_nccl_gather"] = t1 / (world * rec["t_nccl_us"])
+            rec["efficiency_chain_peer_gather"] = t1c / (world * rec["t_peer_chain_us"])
+            ok = True
+            for m in (0, C - 1):
+                ok = ok and bool(torch.equal(peer_out.y[m], Y1[m])) and bool(torch.equal(nccl_out.full(m), Y1[m]))
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            rec["gathered_equal_single_gpu"] = bool(flag.item())
+            all_equal = all_equal and rec["gathered_equal_single_gpu"]
+            assert peer_out.status.cpu().tolist() == [0, 0], "peer-gather status"
+            dist.barrier()
+            torch.cuda.synchronize()
+            peer_out.close()
+            del Wf, Sf
+        assert status.cpu().tolist() == [0, 0], f"device status {status.cpu().tolist()}"
+        out["shapes"][name] = rec
+        del W, S, X, Yl, Y1, peer_out, nccl_out
+        torch.cuda.empty_cache()
+    if world > 1:
+        out["gathered_equal_single_gpu"] = all_equal
+    out["note"] = ("t1 and the efficiencies come from this run (the full matrices all-gathered to every rank and "
+                   "timed on one GPU each); GEMV-only efficiency excludes any gather")
+    return out
 
 
 I8_N, I8_K, I8_SA = 4096, 4096, 0.02

@@ -11,7 +11,10 @@
  *   synchronous  (no suffix)   same as ks_quantized.h: device, managed or
  *                              host pointers; returns when the output is
  *                              written; bad scales reported as
- *                              KS_ERR_INVALID_ARG.
+ *                              KS_ERR_INVALID_ARG with the reference's
+ *                              output contents (rows before the first row
+ *                              with a bad scale written, that row and the
+ *                              later ones left as they were).
  *   asynchronous (_async)      device (or managed) pointers only; the kernel
  *                              is queued on `stream` (a cudaStream_t, NULL for
  *                              the legacy default stream) and the call
@@ -206,11 +209,15 @@ int ks_b200_ipc_close_handle(void *peer_ptr, size_t offset);
  * each, the shape of ks_b200_matvec_w4a8_batch_async).  The output of row r
  * of matrix m is stored at rank_outputs[p][m * matrix_stride + row_offset + r]
  * for every rank p (rank_outputs[p] is that rank's gathered buffer, opened
- * with ks_b200_ipc_open_handle; this rank's own buffer included).  After its
- * last store each CTA adds 1 to every rank's arrival counter
- * (rank_counters[p]), behind a system-scope fence; *signals_per_rank
- * receives how many such arrivals this call sends to each rank.  Needs the
- * streaming kernel's shape rules (else KS_ERR_UNSUPPORTED).
+ * with ks_b200_ipc_open_handle; this rank's own buffer included).  Each CTA
+ * collects its rows of a matrix in shared memory and writes them to every
+ * rank as one contiguous run of coalesced stores once the matrix is done.
+ * After its last store each CTA adds 1 to rank_counters[p] for every rank p,
+ * behind a system-scope fence; give each rank an array of nranks counter
+ * words and pass, as rank_counters[p], the word of rank p's array that
+ * counts this rank's arrivals (see ks_b200_peer_arrival_wait_ranks_async).
+ * *signals_per_rank receives how many arrivals this call sends to each rank.
+ * Needs the streaming kernel's shape rules (else KS_ERR_UNSUPPORTED).
  */
 int ks_b200_matvec_w4a8_batch_gather_async(
     int count, const int8_t *const *inputs,
@@ -233,6 +240,29 @@ int ks_b200_matvec_w4a8_batch_gather_async(
 int ks_b200_peer_arrival_wait_async(const uint32_t *counter,
                                     uint32_t *expected, uint32_t arrivals,
                                     uint32_t *status, void *stream);
+
+/*
+ * The same wait over one counter word per source rank: counters[s] (device
+ * memory on this rank, zero-initialised with expected[0]) counts the
+ * arrivals from rank s.  The wait ends once every counters[s] has received
+ * arrivals_per_rank more signals than at the previous wait, so arrivals a
+ * fast rank sends for its next run cannot stand in for those of a slow rank.
+ * It gives up after timeout_ns nanoseconds (0: one second; at most 10 s),
+ * sets status word 1 and returns; expected[0] advances either way.
+ */
+int ks_b200_peer_arrival_wait_ranks_async(const uint32_t *counters, int nranks,
+                                          uint32_t *expected,
+                                          uint32_t arrivals_per_rank,
+                                          uint64_t timeout_ns, uint32_t *status,
+                                          void *stream);
+
+/*
+ * Synchronise `stream` and turn the status words an asynchronous call wrote
+ * (device, managed or mapped memory) into the synchronous calls' codes:
+ * KS_ERR_DEVICE if a device-side wait timed out, KS_ERR_INVALID_ARG if a
+ * weight scale was <= 0, inf or nan, else KS_OK.  Allocates nothing.
+ */
+int ks_b200_status_check(const uint32_t *status, void *stream);
 
 /*
  * One quantised Llama-style decode layer at batch 1 (no counterpart in the

@@ -173,3 +173,20 @@ def test_layout_version_and_importer_argument_checks(ks):
     assert L.ks_b200_import_ggml_q4_0_async(a, 10, 1, 32, 32, a, 32, a, 0, 1, None) == E
     assert L.ks_b200_import_ggml_q4_0_async(a, 18, 1, 32, 32, a, 8, a, 0, 1, None) == E
     assert L.ks_b200_import_ggml_q4_0_async(a, 18, 1, 32, 32, a, 32, a, 5, 1, None) == E
+
+
+def test_wait_and_status_check_argument_checks(ks):
+    """The bounded peer wait and the status check reject bad arguments on the
+    host, before any CUDA call."""
+    L = ks.lib()
+    buf = np.zeros(64, np.uint32)
+    a = ks.addr(buf)
+    assert L.ks_b200_peer_arrival_wait_ranks_async(None, 2, a, 1, 0, None, None) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_peer_arrival_wait_ranks_async(a, 2, None, 1, 0, None, None) == ks.KS_ERR_INVALID_ARG
+    for nranks in (0, 9, -1):
+        assert L.ks_b200_peer_arrival_wait_ranks_async(a, nranks, a + 128, 1, 0, None, None) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_peer_arrival_wait_ranks_async(a, 2, a + 128, 1, 10_000_000_001, None, None) == \
+        ks.KS_ERR_INVALID_ARG
+    assert "10 s" in ks.last_error()
+    assert L.ks_b200_peer_arrival_wait_async(None, a, 1, None, None) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_status_check(None, None) == ks.KS_ERR_INVALID_ARG

@@ -353,24 +353,67 @@ def test_config_sharded_shapes_rows_sample(ks, cuda, oracle, n):
 # ------------------------------------------------------- semantics ---------
 
 
-def test_bad_scale_returns_invalid_arg(ks, cuda, oracle):
+@pytest.mark.parametrize("f16", [False, True], ids=["f32_scales", "f16_scales"])
+@pytest.mark.parametrize("out_on", ["device", "host"])
+@pytest.mark.parametrize("cols", [1024, 1000], ids=["streaming", "generic"])
+def test_bad_scale_returns_invalid_arg(ks, cuda, oracle, f16, out_on, cols):
+    """A bad scale returns KS_ERR_INVALID_ARG and leaves the WHOLE output buffer
+    as the reference leaves it: rows before the first bad row written, that row
+    and every later one untouched (ks_quantized.c:148-156, scale check :112-114)."""
     import torch
 
-    rows, cols, group = 300, 1024, 32
-    x, w, s, wstride, sstride = make_w4a8(9, rows, cols, group)
-    for bad in (0.0, -1.0, np.inf, np.nan):
+    rows, group = 300, 32
+    x, w, s, wstride, sstride = make_w4a8(9, rows, cols, group, f16=f16)
+    for bad_row, bad in ((211, 0.0), (211, -1.0), (211, np.inf), (211, np.nan), (0, 0.0), (rows - 1, -0.0),
+                         (37, 0.0)):
         s2 = s.copy()
-        s2[211, 7] = bad
-        y = torch.full((rows,), 7.0, dtype=torch.float32, device=cuda)
-        rc = call_matvec_w4a8(ks, dev(x, cuda), dev(w, cuda), wstride, dev(s2, cuda), sstride, y, rows, cols, group, 0.5)
-        assert rc == ks.KS_ERR_INVALID_ARG
-        o = np.full(rows, 7.0, np.float32)
-        rc_ref, _ = oracle.matvec_w4a8(x, w, wstride, s2, sstride, rows, cols, group, 0.5, out=o)
+        s2[bad_row, 7] = bad
+        if bad_row == 37:  # two bad rows: the first one decides
+            s2[250, 1] = np.nan
+        first = 37 if bad_row == 37 else bad_row
+        fill = np.full(rows, 7.0, np.float32)
+        fill[::3] = -2.5  # untouched rows must keep their own contents, not one fill value
+        s_arg = s2.view(np.uint16) if f16 else s2
+        y = dev(fill, cuda) if out_on == "device" else fill.copy()
+        rc = call_matvec_w4a8(ks, dev(x, cuda), dev(w, cuda), wstride, dev(s_arg, cuda), sstride, y, rows, cols,
+                              group, 0.5, f16=f16)
+        assert rc == ks.KS_ERR_INVALID_ARG, (rc, ks.last_error())
+        o = fill.copy()
+        if f16:
+            rc_ref, _ = oracle.matvec_w4a8_f16(x, w, wstride, s_arg, sstride, rows, cols, group, 0.5, out=o)
+        else:
+            rc_ref, _ = oracle.matvec_w4a8(x, w, wstride, s2, sstride, rows, cols, group, 0.5, out=o)
         assert rc_ref == -1
-        assert_w4a8_close(host(y)[:211], o[:211], "rows before the bad row")
-    # the next good call succeeds (status is per call)
+        got = host(y) if out_on == "device" else y
+        if first > 0:
+            assert_w4a8_close(got[:first], o[:first], "rows before the first bad row")
+        np.testing.assert_array_equal(got[first:].view(np.uint32), o[first:].view(np.uint32),
+                                      err_msg=f"rows from the first bad row ({first}) must be untouched")
+    # the next good call succeeds (status is per call) and writes every row
     y = torch.zeros(rows, dtype=torch.float32, device=cuda)
-    assert call_matvec_w4a8(ks, dev(x, cuda), dev(w, cuda), wstride, dev(s, cuda), sstride, y, rows, cols, group, 0.5) == 0
+    s_arg = s.view(np.uint16) if f16 else s
+    assert call_matvec_w4a8(ks, dev(x, cuda), dev(w, cuda), wstride, dev(s_arg, cuda), sstride, y, rows, cols,
+                            group, 0.5, f16=f16) == 0
+    o = np.zeros(rows, np.float32)
+    if f16:
+        oracle.matvec_w4a8_f16(x, w, wstride, s_arg, sstride, rows, cols, group, 0.5, out=o)
+    else:
+        oracle.matvec_w4a8(x, w, wstride, s, sstride, rows, cols, group, 0.5, out=o)
+    assert_w4a8_close(host(y), o, "good call after a bad one")
+
+
+def test_dot_w4a8_bad_scale_leaves_output(ks, cuda):
+    """ks_dot_w4a8 with a bad scale returns KS_ERR_INVALID_ARG and does not write *output."""
+    k, group = 256, 32
+    x, w, s, _, _ = make_w4a8(11, 1, k, group)
+    s[0, 3] = np.nan
+    for out_on in ("device", "host"):
+        out = dev(np.array([42.0], np.float32), cuda) if out_on == "device" else np.array([42.0], np.float32)
+        a = ks.addr
+        rc = ks.lib().ks_dot_w4a8(a(dev(x, cuda)), a(dev(w, cuda)), a(dev(s, cuda)), k, group, 0.5, 0, 0, a(out),
+                                  None, 0)
+        assert rc == ks.KS_ERR_INVALID_ARG
+        assert float((host(out) if out_on == "device" else out)[0]) == 42.0
 
 
 def test_bad_f16_scale(ks, cuda):

@@ -18,6 +18,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "ks_b200.h"
 #include "ks_internal.h"
@@ -27,7 +28,11 @@ namespace ksb {
 namespace {
 
 constexpr int kMaxDevices = 64;
-enum Slot { kSlotX = 0, kSlotW, kSlotS, kSlotY, kSlotS2, kSlots };
+constexpr uint64_t kWaitLimitNsHost = 1000000000ull;  // the kernels' one-second wait limit
+constexpr uint64_t kWaitLimitMaxNs = 10000000000ull;
+// kSlotSnap: the caller's device-resident output rows before a W4A8 call;
+// kSlotAux: the first-bad-row word of the W4A8 error path.
+enum Slot { kSlotX = 0, kSlotW, kSlotS, kSlotY, kSlotS2, kSlotSnap, kSlotAux, kSlots };
 
 struct ThreadState {
   uint32_t *status = nullptr;  // mapped, portable pinned host memory
@@ -35,6 +40,7 @@ struct ThreadState {
     void *p = nullptr;
     size_t n = 0;
   } bufs[kMaxDevices][kSlots];
+  std::vector<unsigned char> host_snap;  // the caller's host-resident output rows before a W4A8 call
   std::string err;
   ~ThreadState() {
     for (int d = 0; d < kMaxDevices; ++d)
@@ -130,13 +136,8 @@ class SyncCall {
     return KS_OK;
   }
 
-  // Device address for buffer i of `bytes` bytes; host buffers are staged
-  // (inputs copied in now, outputs copied back by finish()).
-  int map(int i, int slot, const void *host, size_t bytes, bool input, void **out) {
-    if (where_[i].device || bytes == 0) {
-      *out = const_cast<void *>(host);
-      return KS_OK;
-    }
+  // A thread-local device buffer of at least `bytes` bytes in `slot`.
+  int scratch(int slot, size_t bytes, void **out) {
     ThreadState::Buf &b = tls().bufs[dev_][slot];
     if (b.n < bytes) {
       if (b.p) cudaFree(b.p);
@@ -146,6 +147,24 @@ class SyncCall {
       if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(staging)");
       b.n = bytes;
     }
+    *out = b.p;
+    return KS_OK;
+  }
+
+  bool is_device(int i) const { return where_[i].device; }
+  bool bad_scale() const { return static_cast<const volatile uint32_t *>(tls().status)[kStatusBadScale] != 0; }
+
+  // Device address for buffer i of `bytes` bytes; host buffers are staged
+  // (inputs copied in now, outputs copied back by finish()).
+  int map(int i, int slot, const void *host, size_t bytes, bool input, void **out) {
+    if (where_[i].device || bytes == 0) {
+      *out = const_cast<void *>(host);
+      return KS_OK;
+    }
+    void *p = nullptr;
+    int rc = scratch(slot, bytes, &p);
+    if (rc != KS_OK) return rc;
+    ThreadState::Buf &b = tls().bufs[dev_][slot];
     if (input) {
       cudaError_t e = cudaMemcpyAsync(b.p, host, bytes, cudaMemcpyHostToDevice, 0);
       if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(H2D)");
@@ -240,6 +259,21 @@ int w4a8_sync(const int8_t *x, const uint8_t *w, size_t wstride, const void *s, 
   if ((rc = call.map(1, kSlotW, w, wbytes, true, &dw)) != KS_OK) return rc;
   if ((rc = call.map(2, kSlotS, s, sbytes, true, &ds)) != KS_OK) return rc;
   if ((rc = call.map(3, kSlotY, y, rows * sizeof(float), false, &dy)) != KS_OK) return rc;
+  // The kernels compute every row in one pass, but the reference stops at the
+  // first row with a bad scale and leaves that row and all later ones as they
+  // were (ks_quantized.c:148-156).  Keep the caller's rows, so the error path
+  // below can put them back.
+  const size_t ybytes = rows * sizeof(float);
+  void *snap = nullptr;
+  if (call.is_device(3)) {
+    if ((rc = call.scratch(kSlotSnap, ybytes, &snap)) != KS_OK) return rc;
+    cudaError_t e = cudaMemcpyAsync(snap, y, ybytes, cudaMemcpyDeviceToDevice, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(output snapshot)");
+  } else {
+    std::vector<unsigned char> &hs = tls().host_snap;
+    if (hs.size() < ybytes) hs.resize(ybytes);
+    std::memcpy(hs.data(), y, ybytes);
+  }
   W4A8Launch a{};
   a.x = static_cast<const int8_t *>(dx);
   a.w = static_cast<const uint8_t *>(dw);
@@ -255,7 +289,32 @@ int w4a8_sync(const int8_t *x, const uint8_t *w, size_t wstride, const void *s, 
   a.zx = zx;
   a.zw = zw;
   a.status = call.status_dev();
-  return call.finish(launch_w4a8(a, 0, call.device()));
+  rc = call.finish(launch_w4a8(a, 0, call.device()));
+  if (rc != KS_ERR_INVALID_ARG || !call.bad_scale()) return rc;
+  const std::string msg = tls().err;
+  // Bad scale: find the first failing row and restore it and every later row.
+  void *aux = nullptr;
+  if ((rc = call.scratch(kSlotAux, 256, &aux)) != KS_OK) return rc;
+  unsigned long long first = ~0ull;
+  cudaError_t e = cudaMemsetAsync(aux, 0xFF, sizeof first, 0);
+  if (e == cudaSuccess)
+    e = launch_w4a8_first_bad_row(ds, stype, (int64_t)sstride, (int64_t)rows, (int64_t)groups,
+                                  static_cast<unsigned long long *>(aux), 0);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&first, aux, sizeof first, cudaMemcpyDeviceToHost, 0);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+  if (e != cudaSuccess) return cuda_fail(e, "first bad scale row");
+  if (first < rows) {
+    const size_t off = (size_t)first * sizeof(float);
+    if (call.is_device(3)) {
+      e = cudaMemcpyAsync(reinterpret_cast<unsigned char *>(y) + off, static_cast<unsigned char *>(snap) + off,
+                          ybytes - off, cudaMemcpyDeviceToDevice, 0);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(output restore)");
+    } else {
+      std::memcpy(reinterpret_cast<unsigned char *>(y) + off, tls().host_snap.data() + off, ybytes - off);
+    }
+  }
+  return fail(KS_ERR_INVALID_ARG, msg);
 }
 
 // Checks of ks_matvec_w4a8 (ks_quantized.c:138-146) followed by the per-row
@@ -965,8 +1024,33 @@ extern "C" int ks_b200_matvec_w4a8_batch_gather_async(
 extern "C" int ks_b200_peer_arrival_wait_async(const uint32_t *counter, uint32_t *expected, uint32_t arrivals,
                                                uint32_t *status, void *stream) {
   if (!counter || !expected) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
-  cudaError_t e = launch_peer_wait(counter, expected, arrivals, status, static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_peer_wait(counter, 1, expected, arrivals, kWaitLimitNsHost, status,
+                                   static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_peer_arrival_wait_ranks_async(const uint32_t *counters, int nranks, uint32_t *expected,
+                                                     uint32_t arrivals_per_rank, uint64_t timeout_ns,
+                                                     uint32_t *status, void *stream) {
+  if (!counters || !expected) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (nranks < 1 || nranks > 8) return fail(KS_ERR_INVALID_ARG, "nranks must be 1..8");
+  if (timeout_ns > kWaitLimitMaxNs) return fail(KS_ERR_INVALID_ARG, "timeout_ns above 10 s");
+  cudaError_t e = launch_peer_wait(counters, nranks, expected, arrivals_per_rank,
+                                   timeout_ns ? timeout_ns : kWaitLimitNsHost, status,
+                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
+extern "C" int ks_b200_status_check(const uint32_t *status, void *stream) {
+  if (!status) return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t words[kStatusWords] = {0, 0};
+  e = cudaMemcpy(words, status, sizeof words, cudaMemcpyDefault);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (words[kStatusTimeout]) return fail(KS_ERR_DEVICE, "a device-side wait timed out");
+  if (words[kStatusBadScale]) return fail(KS_ERR_INVALID_ARG, "a weight scale is <= 0, inf or nan");
+  return KS_OK;
 }
 
 // ================================================================ decode layer

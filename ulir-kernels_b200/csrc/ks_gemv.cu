@@ -61,7 +61,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + g.nst;
   uint8_t *xbufs = smem + kBarBytes;
-  uint8_t *stages = xbufs + 2 * g.xbuf_bytes;
+  float *ostage = reinterpret_cast<float *>(xbufs + 2 * g.xbuf_bytes);  // 2 buffers (peer gather only)
+  uint8_t *stages = xbufs + 2 * g.xbuf_bytes + 2 * g.ostage_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -188,7 +189,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
   bool stop = false;  // this warp hit a wait limit: it skips work but keeps every barrier
   for (int m = 0; m < g.count; ++m) {
     const GemvItem &it = items.it[m];
-    const OutRef out{it.y, &items, (int64_t)m * items.mstride + items.row_offset, &ext, m};
+    float *ost = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ostage) + (size_t)(m & 1) * g.ostage_bytes);
+    const OutRef out{it.y, &items, (int64_t)m * items.mstride + items.row_offset, &ext, m, ost, r0};
     // f32 inputs: one vector (ext.xf) for every matrix of the launch, prepared once
     const uint8_t *xb = xbufs + (ext.xmode != kXInt8 ? 0 : (size_t)(m & 1) * g.xbuf_bytes);
     uint32_t pre[2][RW];
@@ -251,6 +253,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
       }
       consumers_sync<CW>();  // every consumer warp, stopped or not, takes this barrier
     }
+    if (items.npeers > 0) {
+      // the matrix's rows are all staged once every consumer passed a barrier
+      // after them; the other staging buffer takes the next matrix's rows
+      if (!more) consumers_sync<CW>();
+      flush_peer_rows<CW>(items, ost, out.peer_off + r0, rows_cta, ctid);
+    }
   }
   if (__any_sync(0xffffffffu, Op::bad(mx)) && lane == 0) set_status(g.status, kStatusBadScale);
   if (items.npeers > 0) {
@@ -264,25 +272,34 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW <= 8 ? 2 : 1)
   }
 }
 
-// Waits until this rank's arrival counter reaches the running target: the
-// target (kept in expected[0]) grows by `arrivals` per call -- the number of
-// CTA signals the preceding sharded launches send to every rank.  Bounded by
-// the one-second wait limit; a timeout sets status word 1.
-__global__ void peer_arrival_wait_kernel(const uint32_t *counter, uint32_t *expected, uint32_t arrivals,
-                                         uint32_t *status) {
-  if (threadIdx.x != 0) return;
+// Waits until each of this rank's `ncounters` arrival counters (one word per
+// source rank) reaches the running target: the target (kept in expected[0])
+// grows by `arrivals` per call -- the number of CTA signals the preceding
+// sharded launches send from each source.  Lane s polls counter s.  A
+// separate word per source means a fast rank's arrivals for the next run
+// can never stand in for a slow rank's arrivals for this one.  Bounded by
+// limit_ns of %globaltimer; a timeout sets status word 1 and the kernel
+// returns (expected[0] still advances, so the next call targets the next
+// run).
+__global__ void peer_arrival_wait_kernel(const uint32_t *counters, int ncounters, uint32_t *expected,
+                                         uint32_t arrivals, uint64_t limit_ns, uint32_t *status) {
+  const int lane = threadIdx.x;
   const uint32_t target = expected[0] + arrivals;
-  expected[0] = target;
+  bool done = lane >= ncounters;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
-    if ((int32_t)(v - target) >= 0) break;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      set_status(status, kStatusTimeout);
+  while (!__all_sync(0xffffffffu, done)) {
+    if (!done) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(counters + lane) : "memory");
+      done = (int32_t)(v - target) >= 0;
+    }
+    if (globaltimer_ns() - t0 > limit_ns) {
+      if (lane == 0) set_status(status, kStatusTimeout);
       break;
     }
   }
+  __syncwarp();
+  if (lane == 0) expected[0] = target;
 }
 
 // ------------------------------------------------------- generic kernels --
@@ -313,6 +330,25 @@ __global__ void __launch_bounds__(256)
     if (lane == 0) y[r] = acc * sx;
   }
   if (__any_sync(0xffffffffu, bad) && lane == 0) set_status(status, kStatusBadScale);
+}
+
+// Error path of the synchronous W4A8 calls: the reference stops at the first
+// row whose scales fail validation (ks_quantized.c:148-156 with :112-114), so
+// the library needs that row's index.  A warp per row tests the row's
+// `groups` scales with the kernels' own bit test; the smallest failing row
+// wins (atomicMin).
+template <typename ST>
+__global__ void __launch_bounds__(256)
+    w4a8_first_bad_row_kernel(const ST *__restrict__ s, int64_t sstride, int64_t rows, int64_t groups,
+                              unsigned long long *first_bad) {
+  using SB = ScaleBits<ST>;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nwarps) {
+    bool bad = false;
+    for (int64_t gi = lane; gi < groups; gi += 32) bad |= SB::bad(SB::gload(s + r * sstride + gi));
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicMin(first_bad, (unsigned long long)r);
+  }
 }
 
 template <bool OUT_F32>
@@ -360,8 +396,10 @@ int ilog2_exact(int64_t v) {
 // l2_ahead: L2 prefetch distance in stages (measured best on B200: W4A8 1
 // single / 2 batched, INT8 1 single / 0 batched; farther prefetches compete
 // with the ring's own copies).
+// peer: the launch gathers its outputs by peer stores and stages each
+// matrix's rows in two shared-memory buffers of rows_cta_max floats.
 bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int xbuf_bytes, int sm_count,
-                 bool batch, int cw, int l2_ahead) {
+                 bool batch, int cw, int l2_ahead, bool peer = false) {
   static const int min_single = std::max(2, env_int("KS_B200_MIN_STAGES", 2));
   static const int ahead_single = env_int("KS_B200_L2_AHEAD_SINGLE", -1);
   static const int ahead_batch = env_int("KS_B200_L2_AHEAD_BATCH", -1);
@@ -369,10 +407,12 @@ bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int
   static const int min_batch_env = env_int("KS_B200_BATCH_MIN_STAGES", -1);
   const int smem_cta = batch ? kSmemBatch : kSmemSingle;
   const int row_total = row_bytes + srow_bytes;
-  const int budget = smem_cta - kBarBytes - 2 * xbuf_bytes;
-  if (budget <= 0) return false;
   const int64_t n_cta = std::min<int64_t>(rows, sm_count);
   const int64_t rows_cta_max = (rows + n_cta - 1) / n_cta;
+  const int64_t ostage = peer ? (rows_cta_max * 4 + 127) / 128 * 128 : 0;
+  if (ostage > smem_cta / 8) return false;
+  const int budget = smem_cta - kBarBytes - 2 * xbuf_bytes - 2 * (int)ostage;
+  if (budget <= 0) return false;
   int rps;
   const int64_t half = budget / 2;
   const int64_t bytes_cta = rows_cta_max * (int64_t)row_total;  // one matrix, one CTA
@@ -406,13 +446,14 @@ bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int
   g.srow_bytes = srow_bytes;
   g.stage_bytes = stage_bytes;
   g.xbuf_bytes = xbuf_bytes;
+  g.ostage_bytes = (int32_t)ostage;
   const int ahead_env = batch ? ahead_batch : ahead_single;
   g.l2_ahead = ahead_env >= 0 ? ahead_env : l2_ahead;
   return true;
 }
 
 size_t stream_smem_bytes(const StreamGeom &g) {
-  return (size_t)kBarBytes + 2 * (size_t)g.xbuf_bytes + (size_t)g.nst * g.stage_bytes;
+  return (size_t)kBarBytes + 2 * (size_t)g.xbuf_bytes + 2 * (size_t)g.ostage_bytes + (size_t)g.nst * g.stage_bytes;
 }
 
 template <class Op, int CW>
@@ -461,7 +502,7 @@ bool w4a8_shape_ok(const W4A8Launch &a) {
          (a.sstride * ssize) % 16 == 0 && a.rows < (int64_t(1) << 31);
 }
 
-W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch) {
+W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch, bool peer = false) {
   W4A8Plan P;
   if (!w4a8_shape_ok(a)) return P;
   const int ssize = a.stype == kScaleF16 ? 2 : 4;
@@ -470,7 +511,7 @@ W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch) {
   const int xbuf = ((chunks * 36 + 4 + 127) / 128) * 128;
   StreamGeom g{};
   if (!plan_stream(g, a.rows, (int)(a.cols / 2), (int)(groups * ssize), xbuf, device_props(device).sm_count,
-                   batch, batch ? 16 : 8, batch ? 2 : 1))
+                   batch, batch ? 16 : 8, batch ? 2 : 1, peer))
     return P;
   g.wstride = a.wstride;
   g.sstride = a.sstride * ssize;
@@ -585,6 +626,18 @@ cudaError_t launch_w4a8_generic(const W4A8Launch &a, cudaStream_t stream, int de
         a.x, a.w, a.wstride, reinterpret_cast<const float *>(a.s), a.sstride, a.y, a.rows, a.cols, a.group,
         a.sx, a.zx, a.zw, a.status);
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_first_bad(const void *s, int stype, int64_t sstride, int64_t rows, int64_t groups,
+                             unsigned long long *first_bad, cudaStream_t stream, int device) {
+  const int grid = generic_grid(rows, device_props(device).sm_count);
+  if (stype == kScaleF16)
+    w4a8_first_bad_row_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(s), sstride, rows,
+                                                                groups, first_bad);
+  else
+    w4a8_first_bad_row_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float *>(s), sstride, rows,
+                                                               groups, first_bad);
   return cudaGetLastError();
 }
 
@@ -764,7 +817,7 @@ cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b
   if (pg.npeers < 1 || pg.npeers > kMaxPeers) return cudaErrorInvalidValue;
   if (b.count <= 0) return cudaSuccess;
   if (!batch_aligned(b, true)) return cudaErrorInvalidValue;
-  W4A8Plan P = plan_w4a8(shape, device, b.count > 1);
+  W4A8Plan P = plan_w4a8(shape, device, b.count > 1, /*peer=*/true);
   if (!P.fast) return cudaErrorInvalidValue;
   for (int i0 = 0; i0 < b.count; i0 += kMaxItems) {
     const int n = std::min(kMaxItems, b.count - i0);
@@ -790,9 +843,17 @@ cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b
   return cudaSuccess;
 }
 
-cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32_t arrivals, uint32_t *status,
-                             cudaStream_t stream) {
-  peer_arrival_wait_kernel<<<1, 32, 0, stream>>>(counter, expected, arrivals, status);
+cudaError_t launch_w4a8_first_bad_row(const void *s, int stype, int64_t sstride, int64_t rows, int64_t groups,
+                                      unsigned long long *first_bad, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return launch_first_bad(s, stype, sstride, rows, groups, first_bad, stream, dev);
+}
+
+cudaError_t launch_peer_wait(const uint32_t *counters, int ncounters, uint32_t *expected, uint32_t arrivals,
+                             uint64_t limit_ns, uint32_t *status, cudaStream_t stream) {
+  if (ncounters < 1 || ncounters > 32) return cudaErrorInvalidValue;
+  peer_arrival_wait_kernel<<<1, 32, 0, stream>>>(counters, ncounters, expected, arrivals, limit_ns, status);
   return cudaGetLastError();
 }
 

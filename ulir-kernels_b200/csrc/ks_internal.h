@@ -138,10 +138,14 @@ cudaError_t launch_decode_layer_w4a8(const DecodeLayerArgs &a, cudaStream_t stre
 cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device,
                                            bool dry = false);
 
-// Wait (bounded) until *counter reaches expected[0] + arrivals; expected[0]
-// then holds the new target.
-cudaError_t launch_peer_wait(const uint32_t *counter, uint32_t *expected, uint32_t arrivals, uint32_t *status,
-                             cudaStream_t stream);
+// Wait (bounded by limit_ns) until each of counters[0 .. ncounters) reaches
+// expected[0] + arrivals; expected[0] then holds the new target.
+cudaError_t launch_peer_wait(const uint32_t *counters, int ncounters, uint32_t *expected, uint32_t arrivals,
+                             uint64_t limit_ns, uint32_t *status, cudaStream_t stream);
+// First row r (of `rows`) whose scale row holds a scale <= 0, inf or nan,
+// into *first_bad (atomicMin; the caller sets it to ~0 first).
+cudaError_t launch_w4a8_first_bad_row(const void *s, int stype, int64_t sstride, int64_t rows, int64_t groups,
+                                      unsigned long long *first_bad, cudaStream_t stream);
 cudaError_t launch_gemm_i8(const GemmI8Launch &a, cudaStream_t stream, int device);
 
 // Independent GEMMs of one shape (m, n, k, strides and out_scale from the

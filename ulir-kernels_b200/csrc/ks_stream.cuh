@@ -32,8 +32,13 @@ constexpr int kMaxPeers = 8;
 // Per-launch matrix list.  When npeers > 0 the launch is a sharded GEMV whose
 // outputs are gathered by peer stores: the output of row r of matrix m goes to
 // peer_y[p][m * mstride + row_offset + r] of every rank p (this rank
-// included), and after its last store each CTA adds 1 to every rank's
-// arrival counter peer_cnt[p] (system scope, after a system-scope fence).
+// included).  A CTA collects its rows of a matrix in shared memory and, once
+// the matrix is done, its consumer threads write that contiguous slice to
+// every rank with coalesced stores (a warp writes 128 consecutive bytes of
+// one rank's buffer per instruction, instead of one 4-byte NVLink write per
+// row and rank).  After its last store each CTA adds 1 to peer_cnt[p] for
+// every rank p (system scope, after a system-scope fence); peer_cnt[p] is
+// the word of rank p's counter array that counts this rank's arrivals.
 struct GemvItems {
   GemvItem it[kMaxItems];
   float *peer_y[kMaxPeers];
@@ -79,6 +84,8 @@ struct OutRef {
   int64_t peer_off;      // m * mstride + row_offset
   const LayerExt *ext;
   int m;
+  float *ostage;         // npeers > 0: this CTA's rows of matrix m, in shared memory
+  int64_t r0;            // first row of this CTA
   // the epilogue's global operand for row r (residual or gate value), loaded
   // before the row's dot product
   struct Pre {
@@ -110,7 +117,23 @@ __device__ __forceinline__ void store_f32(const OutRef &o, int64_t r, float v, O
     }
     reinterpret_cast<float *>(o.y)[r] = out;
   } else {
-    for (int p = 0; p < np; ++p) o.items->peer_y[p][o.peer_off + r] = v;
+    o.ostage[r - o.r0] = v;  // written to the ranks by flush_peer_rows
+  }
+}
+
+// Write this CTA's staged rows [r0, r0 + n) of one matrix to every rank's
+// gathered buffer: consecutive threads take consecutive rows of one rank, so
+// each warp store instruction covers up to 128 contiguous bytes.  Every
+// consumer thread calls it after the consumer barrier that follows the
+// matrix's last row.
+template <int CW>
+__device__ __forceinline__ void flush_peer_rows(const GemvItems &items, const float *ostage, int64_t off, int n,
+                                                int ctid) {
+  const int total = n * items.npeers;
+  for (int i = ctid; i < total; i += CW * 32) {
+    const int p = i / n;
+    const int e = i - p * n;
+    items.peer_y[p][off + e] = ostage[e];
   }
 }
 
@@ -129,6 +152,7 @@ struct StreamGeom {
   int32_t srow_bytes;   // streamed bytes per side row (0: none)
   int32_t stage_bytes;
   int32_t xbuf_bytes;   // one prepared-activation buffer
+  int32_t ostage_bytes; // one output staging buffer (peer-gather launches; else 0)
   int32_t w_contig;     // wstride == row_bytes: one copy per stage
   int32_t s_contig;
   int32_t x_al16;       // every activation vector 16-byte aligned

@@ -98,6 +98,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          _vp, _vp],
     ),
     "ks_b200_peer_arrival_wait_async": (c_int, [_vp, _vp, c_uint32, _vp, _vp]),
+    "ks_b200_peer_arrival_wait_ranks_async": (c_int, [_vp, c_int, _vp, c_uint32, ctypes.c_uint64, _vp, _vp]),
+    "ks_b200_status_check": (c_int, [_vp, _vp]),
     "ks_b200_decode_layer_workspace": (_sz, [_sz, _sz]),
     "ks_b200_decode_layer_offsets": (c_int, [_sz, _sz, _vp]),
     "ks_b200_decode_layer_w4a8_async": (

@@ -114,15 +114,20 @@ class PeerGatherW4A8:
     and a gathered buffer `y` of shape [count, world * rows]: after `run()` and
     the arrival wait it queues, y[m] is the full output of matrix m on every
     rank.  The buffers are exchanged once with CUDA IPC; the data path is the
-    GEMV kernel's own stores plus a one-thread arrival wait -- no collective
-    library.  Use two instances (or alternate buffers) when a consumer of y may
-    still be reading while the next run starts.
+    GEMV kernel's own stores plus a one-warp arrival wait -- no collective
+    library.  Each rank keeps one arrival counter word per source rank
+    (`sync[s]` counts the CTA signals from rank s), so the wait checks every
+    source separately.  Use two instances (or alternate buffers) when a
+    consumer of y may still be reading while the next run starts.
 
     Create and close on every rank in the same order (the constructor runs one
-    all_gather_object on `group`).
+    all_gather_object on `group`).  `timeout_ns` bounds each wait (0: the
+    library's one second).
     """
 
-    def __init__(self, count: int, rows: int, device, group=None):
+    EXPECTED_WORD = 32  # sync[0:world]: counters per source rank; sync[32]: the wait's running target
+
+    def __init__(self, count: int, rows: int, device, group=None, timeout_ns: int = 0):
         import torch
         import torch.distributed as dist
 
@@ -132,9 +137,9 @@ class PeerGatherW4A8:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.count, self.rows = count, rows
+        self.timeout_ns = timeout_ns
         self.y = torch.zeros((count, self.world * rows), dtype=torch.float32, device=device)
-        # word 0: arrival counter (written by every rank), word 1: wait target
-        self.sync = torch.zeros(2, dtype=torch.int32, device=device)
+        self.sync = torch.zeros(64, dtype=torch.int32, device=device)
         self.status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=device)
         mine = []
         for t in (self.y, self.sync):
@@ -152,7 +157,7 @@ class PeerGatherW4A8:
         for p in range(self.world):
             if p == self.rank:
                 y_ptrs.append(self.y.data_ptr())
-                c_ptrs.append(self.sync.data_ptr())
+                c_ptrs.append(self.sync.data_ptr() + 4 * self.rank)
                 continue
             ptrs = []
             for hb, off in everyone[p]:
@@ -162,7 +167,7 @@ class PeerGatherW4A8:
                 self._opened.append((out.value, off))
                 ptrs.append(out.value)
             y_ptrs.append(ptrs[0])
-            c_ptrs.append(ptrs[1])
+            c_ptrs.append(ptrs[1] + 4 * self.rank)  # rank p's word for arrivals from this rank
         self._y_ptrs = list(y_ptrs)
         self._c_ptrs = (ctypes.c_void_p * self.world)(*c_ptrs)
 
@@ -192,11 +197,65 @@ class PeerGatherW4A8:
     def wait(self, signals_per_rank: int, stream=None) -> None:
         """Queue the wait for every rank's signals of the preceding runs."""
         K = self.K
-        K.check(K.lib().ks_b200_peer_arrival_wait_async(
-            self.sync.data_ptr(), self.sync.data_ptr() + 4, self.world * signals_per_rank,
-            K.addr(self.status), K.stream_handle(stream)))
+        K.check(K.lib().ks_b200_peer_arrival_wait_ranks_async(
+            self.sync.data_ptr(), self.world, self.sync.data_ptr() + 4 * self.EXPECTED_WORD, signals_per_rank,
+            self.timeout_ns, K.addr(self.status), K.stream_handle(stream)))
 
     def close(self) -> None:
         for ptr, off in self._opened:
             self.K.lib().ks_b200_ipc_close_handle(ptr, off)
         self._opened = []
+
+
+class NcclGatherW4A8:
+    """The same sharded W4A8 batch with the output slices gathered by NCCL.
+
+    Each rank computes its rows of `count` matrices into `y_local` [count,
+    rows] with one batched GEMV launch on `stream`, then
+    `all_gather_into_tensor` (on `comm_stream` if given, after the launch)
+    fills `y_all` [world, count, rows]: full(m) is matrix m's full output.
+    Every rank issues the same collectives in the same order.
+    """
+
+    def __init__(self, count: int, rows: int, device, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.count, self.rows = count, rows
+        self.y_local = torch.zeros((count, rows), dtype=torch.float32, device=device)
+        self.y_all = torch.zeros((self.world, count, rows), dtype=torch.float32, device=device)
+        self.status = None
+
+    def run(self, xs, ws, ss, cols, group, sx, scale_type, stream=None, comm_stream=None, status=None,
+            w_stride=None, s_stride=None) -> None:
+        import torch
+        import torch.distributed as dist
+
+        import kernelsmith_b200 as K
+
+        n = len(xs)
+        assert n <= self.count
+        K.matvec_w4a8_batch_async(xs, ws, ss, [self.y_local[m] for m in range(n)], w_stride or cols // 2,
+                                  s_stride or -(-cols // group), self.rows, cols, group, sx, scale_type=scale_type,
+                                  status=status, stream=stream)
+        cur = stream or torch.cuda.current_stream()
+        if self.world == 1:
+            with torch.cuda.stream(cur):
+                self.y_all[0].copy_(self.y_local)
+            return
+        if comm_stream is None:
+            with torch.cuda.stream(cur):
+                dist.all_gather_into_tensor(self.y_all, self.y_local, group=self.group)
+            return
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        comm_stream.wait_event(ev)
+        with torch.cuda.stream(comm_stream):
+            dist.all_gather_into_tensor(self.y_all, self.y_local, group=self.group)
+
+    def full(self, m: int):
+        """Matrix m's gathered output, [world * rows] (a copy)."""
+        return self.y_all[:, m, :].reshape(-1)
