@@ -727,7 +727,10 @@ def layer_bytes(h=LAYER_H, i=LAYER_I, group=GROUP):
 
 def run_decode_layers(K, torch, dev, args):
     """A chain of fused W4A8 decode layers (hidden 4096, inter 11008, G 32,
-    distinct random weights per layer), graph-captured; per-layer time."""
+    distinct random weights per layer), graph-captured; per-layer time.  The
+    headline form is ks_b200_decode_layers_w4a8_async (the whole chain in one
+    call: one persistent launch per 32 layers); one_launch_per_layer is the
+    same chain as one ks_b200_decode_layer_w4a8_async call per layer."""
     import ctypes
 
     L = K.lib()
@@ -743,47 +746,46 @@ def run_decode_layers(K, torch, dev, args):
     norms = torch.rand((2, h), device=dev, generator=gen) + 0.5
     acts = torch.zeros((n + 1, h), dtype=torch.float32, device=dev)
     acts[0].uniform_(-1, 1, generator=gen)
-    ws_bytes = L.ks_b200_decode_layer_workspace(h, i)
+    out = torch.zeros(h, dtype=torch.float32, device=dev)
+    ws_bytes = L.ks_b200_decode_layers_workspace(h, i)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     status = torch.zeros(K.STATUS_WORDS, dtype=torch.int32, device=dev)
     wp = [(ctypes.c_void_p * 5)(*[t.data_ptr() for t in W]) for W in Ws]
     sp = [(ctypes.c_void_p * 5)(*[t.data_ptr() for t in S]) for S in Ss]
+    w_all = (ctypes.c_void_p * (5 * n))(*[t.data_ptr() for W in Ws for t in W])
+    s_all = (ctypes.c_void_p * (5 * n))(*[t.data_ptr() for S in Ss for t in S])
+    n1 = (ctypes.c_void_p * n)(*([norms[0].data_ptr()] * n))
+    n2 = (ctypes.c_void_p * n)(*([norms[1].data_ptr()] * n))
     stream = torch.cuda.Stream(device=dev)
     # the zero-filled workspace and the inputs are written on the current
     # stream; the layers run on `stream`
     stream.wait_stream(torch.cuda.current_stream(dev))
 
-    def chain():
+    def chain_one_call():
+        K.check(L.ks_b200_decode_layers_w4a8_async(n, acts[0].data_ptr(), out.data_ptr(), n1, n2, 1e-5, w_all, s_all,
+                                                    h, i, GROUP, ws.data_ptr(), ws_bytes, status.data_ptr(),
+                                                    K.stream_handle(stream)))
+
+    def chain_per_layer():
         for l in range(n):
             K.check(L.ks_b200_decode_layer_w4a8_async(acts[l].data_ptr(), acts[l + 1].data_ptr(),
                                                       norms[0].data_ptr(), norms[1].data_ptr(), 1e-5, wp[l], sp[l],
                                                       h, i, GROUP, ws.data_ptr(), ws_bytes, status.data_ptr(),
                                                       K.stream_handle(stream)))
 
-    with torch.cuda.stream(stream):
-        chain()
-    stream.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        chain()
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            g.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = 10
-        e0.record(stream)
-        for _ in range(reps):
-            g.replay()
-        e1.record(stream)
-        e1.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / (reps * n)
-    del g
+    us = _graph_us(torch, stream, chain_one_call, n)
+    us_per = _graph_us(torch, stream, chain_per_layer, n)
+    same = bool(torch.equal(out, acts[n]))
     assert status.cpu().tolist() == [0, 0]
     peak, _ = measured_hbm_peak()
     b = layer_bytes()
     return {"layers": n, "us_per_layer": us, "weight_bytes_per_layer": b, "GB_s": b / us / 1e3,
-            "frac": b / us / 1e3 / peak, "launches_per_layer": L.ks_b200_decode_layer_launches(h, i, GROUP),
-            "shape": "hidden 4096, inter 11008, W4A8 G32 f16 scales, batch 1, fused RMSNorm/quantise/SiLU/residual"}
+            "frac": b / us / 1e3 / peak, "launches": -(-n // 32),
+            "one_launch_per_layer": {"us_per_layer": us_per, "frac": b / us_per / 1e3 / peak,
+                                     "launches_per_layer": L.ks_b200_decode_layer_launches(h, i, GROUP)},
+            "chain_equals_per_layer_calls": same,
+            "shape": "hidden 4096, inter 11008, W4A8 G32 f16 scales, batch 1, fused RMSNorm/quantise/SiLU/residual",
+            "api": "ks_b200_decode_layers_w4a8_async (32 layers per persistent launch)"}
 
 
 def _graph_us(torch, stream, fn, units, reps=10, before_timing=None):

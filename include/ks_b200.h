@@ -314,6 +314,35 @@ int ks_b200_decode_layer_w4a8_async(const float *h_in, float *h_out,
                                     void *stream);
 
 /*
+ * A chain of n_layers such layers (no counterpart in the reference): layer l
+ * takes the previous layer's output (h_in for layer 0) and the last layer
+ * writes h_out.  Per layer l: norm1_w[l], norm2_w[l], and the five matrices
+ * weights[5 * l + k] / scales_f16[5 * l + k] in the order qkv, o, gate, up,
+ * down (host arrays of device pointers).  Every layer's results are bitwise
+ * those of ks_b200_decode_layer_w4a8_async on the same input.  Up to 32
+ * layers run in one cooperative persistent launch: the producer warp
+ * streams the next layer's weights while the current layer finishes, so the
+ * launch and the drain of the weight ring are paid once per 32 layers, not
+ * per layer.  workspace: ks_b200_decode_layers_workspace bytes (the
+ * single-layer regions at the offsets ks_b200_decode_layer_offsets gives,
+ * then two f32[hidden] vectors for the outputs of the inner layers; after
+ * the call they hold those of the last two layers before the final one),
+ * zero-filled before its first use; it may not be shared by calls that
+ * can run at the same time.  The intermediates left in it are the last
+ * layer's.  Shape rules, fallback and status as for the single layer.
+ */
+size_t ks_b200_decode_layers_workspace(size_t hidden, size_t inter);
+int ks_b200_decode_layers_w4a8_async(size_t n_layers, const float *h_in,
+                                     float *h_out, const float *const *norm1_w,
+                                     const float *const *norm2_w, float eps,
+                                     const uint8_t *const *weights,
+                                     const uint16_t *const *scales_f16,
+                                     size_t hidden, size_t inter,
+                                     size_t group_size, void *workspace,
+                                     size_t workspace_bytes, uint32_t *status,
+                                     void *stream);
+
+/*
  * Skinny INT8 GEMM with requantisation (batched decode, M = 1..256 tokens):
  *   acc[m, n] = sum_k a[m, k] * w[n, k]                       (int32, exact)
  *   out[m, n] = sat_i8(rne(((f32(acc) * a_scales[m]) * w_scales[n]) / out_scale))

@@ -190,3 +190,26 @@ def test_wait_and_status_check_argument_checks(ks):
     assert "10 s" in ks.last_error()
     assert L.ks_b200_peer_arrival_wait_async(None, a, 1, None, None) == ks.KS_ERR_INVALID_ARG
     assert L.ks_b200_status_check(None, None) == ks.KS_ERR_INVALID_ARG
+
+
+def test_decode_layers_argument_checks(ks):
+    """The layer-chain entry point checks its arguments on the host, in the
+    single-layer call's order, and needs the larger workspace."""
+    import ctypes
+
+    L = ks.lib()
+    h, i = 4096, 11008
+    one = L.ks_b200_decode_layer_workspace(h, i)
+    assert L.ks_b200_decode_layers_workspace(h, i) == one + 2 * 16384
+    buf = np.zeros(64, np.float32)
+    a = ks.addr(buf)
+    ptrs = (ctypes.c_void_p * 10)(*([a] * 10))
+    norms = (ctypes.c_void_p * 2)(a, a)
+    args = [norms, norms, 1e-5, ptrs, ptrs, h, i, 32, a]
+    assert L.ks_b200_decode_layers_w4a8_async(0, a, a, *args, one + 32768, None, None) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_decode_layers_w4a8_async(2, a, a, *args, one, None, None) == ks.KS_ERR_WORKSPACE
+    bad = (ctypes.c_void_p * 10)(*([a] * 9 + [None]))
+    assert L.ks_b200_decode_layers_w4a8_async(2, a, a, norms, norms, 1e-5, bad, ptrs, h, i, 32, a, one + 32768,
+                                              None, None) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_decode_layers_w4a8_async(2, a, a, norms, norms, 0.0, ptrs, ptrs, h, i, 32, a, one + 32768,
+                                              None, None) == ks.KS_ERR_INVALID_ARG

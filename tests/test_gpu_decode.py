@@ -152,3 +152,56 @@ def test_end_to_end_against_oracle_chain(layer, oracle):
     # The few one-step quantisation flips at the two RMSNorms propagate; the
     # layer output stays within 1e-4 of max(|y|, rms(y)).
     _close(y, ref["h_out"], "h_out end to end")
+
+
+@pytest.mark.parametrize("path", ["persistent", "four_launches"])
+@pytest.mark.parametrize("n_layers", [3, 33])
+def test_layer_chain_bitwise_equals_single_layer_calls(ks, cuda, path, n_layers, monkeypatch):
+    """ks_b200_decode_layers_w4a8_async runs n layers (33 crosses the
+    32-layers-per-launch split) and must give bitwise the output of n
+    single-layer calls, each fed the previous one's output."""
+    import ctypes
+
+    import torch
+
+    monkeypatch.setenv("KS_B200_DECODE_PERSISTENT", "1" if path == "persistent" else "0")
+    L = ks.lib()
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(777)
+    shapes = [(3 * H, H), (H, H), (I, H), (I, H), (H, I)]
+    # three distinct weight sets, cycled over the layers; distinct norms per layer
+    sets = [([torch.randint(0, 256, (r, c // 2), dtype=torch.uint8, device=cuda, generator=gen) for r, c in shapes],
+             [(torch.rand((r, c // G), device=cuda, generator=gen) * 9e-3 + 1e-3).half() for r, c in shapes])
+            for _ in range(3)]
+    norms = torch.rand((n_layers, 2, H), device=cuda, generator=gen) + 0.5
+    h0 = torch.rand(H, device=cuda, generator=gen) * 2 - 1
+    wl = [sets[l % 3][0][k].data_ptr() for l in range(n_layers) for k in range(5)]
+    sl = [sets[l % 3][1][k].data_ptr() for l in range(n_layers) for k in range(5)]
+    status = torch.zeros(2, dtype=torch.int32, device=cuda)
+    # the chain in one call
+    ws_bytes = L.ks_b200_decode_layers_workspace(H, I)
+    assert ws_bytes >= L.ks_b200_decode_layer_workspace(H, I) + 2 * H * 4
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=cuda)
+    out = torch.zeros(H, dtype=torch.float32, device=cuda)
+    torch.cuda.synchronize()
+    ks.check(L.ks_b200_decode_layers_w4a8_async(
+        n_layers, h0.data_ptr(), out.data_ptr(), (ctypes.c_void_p * n_layers)(*[norms[l, 0].data_ptr() for l in
+                                                                                 range(n_layers)]),
+        (ctypes.c_void_p * n_layers)(*[norms[l, 1].data_ptr() for l in range(n_layers)]), EPS,
+        (ctypes.c_void_p * (5 * n_layers))(*wl), (ctypes.c_void_p * (5 * n_layers))(*sl), H, I, G, ws.data_ptr(),
+        ws_bytes, status.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    # the same layers one call each
+    ws1 = torch.zeros(L.ks_b200_decode_layer_workspace(H, I), dtype=torch.uint8, device=cuda)
+    acts = torch.zeros((n_layers + 1, H), dtype=torch.float32, device=cuda)
+    acts[0] = h0
+    for l in range(n_layers):
+        ks.check(L.ks_b200_decode_layer_w4a8_async(
+            acts[l].data_ptr(), acts[l + 1].data_ptr(), norms[l, 0].data_ptr(), norms[l, 1].data_ptr(), EPS,
+            (ctypes.c_void_p * 5)(*wl[5 * l:5 * l + 5]), (ctypes.c_void_p * 5)(*sl[5 * l:5 * l + 5]), H, I, G,
+            ws1.data_ptr(), ws1.numel(), status.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    assert torch.isfinite(out).all() and out.abs().max() > 0
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), acts[n_layers].cpu().numpy().view(np.uint32))

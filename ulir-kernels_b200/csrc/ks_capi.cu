@@ -1131,6 +1131,73 @@ extern "C" int ks_b200_decode_layer_w4a8_async(const float *h_in, float *h_out, 
   return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
 }
 
+extern "C" size_t ks_b200_decode_layers_workspace(size_t hidden, size_t inter) {
+  // the single-layer regions, then the two inter-layer activation vectors
+  return ks_b200_decode_layer_workspace(hidden, inter) + 2 * ((hidden * 4 + 255) / 256 * 256);
+}
+
+extern "C" int ks_b200_decode_layers_w4a8_async(size_t n_layers, const float *h_in, float *h_out,
+                                                const float *const *norm1_w, const float *const *norm2_w,
+                                                float eps, const uint8_t *const *weights,
+                                                const uint16_t *const *scales_f16, size_t hidden, size_t inter,
+                                                size_t group_size, void *workspace, size_t workspace_bytes,
+                                                uint32_t *status, void *stream) {
+  if (!h_in || !h_out || !norm1_w || !norm2_w || !weights || !scales_f16 || !workspace)
+    return fail(KS_ERR_INVALID_ARG, "NULL pointer");
+  if (n_layers == 0 || n_layers > 65536) return fail(KS_ERR_INVALID_ARG, "n_layers must be 1..65536");
+  for (size_t l = 0; l < n_layers; ++l) {
+    if (!norm1_w[l] || !norm2_w[l]) return fail(KS_ERR_INVALID_ARG, "NULL RMSNorm weight vector");
+    for (int k = 0; k < 5; ++k)
+      if (!weights[5 * l + k] || !scales_f16[5 * l + k])
+        return fail(KS_ERR_INVALID_ARG, "NULL weight or scale matrix");
+  }
+  if (!pos_finite(eps)) return fail(KS_ERR_INVALID_ARG, "eps must be > 0 and finite");
+  if (hidden == 0 || inter == 0 || hidden % 32 || inter % 32 || group_size < 32 || group_size % 32 ||
+      (group_size & (group_size - 1)) || hidden % group_size || inter % group_size)
+    return fail(KS_ERR_INVALID_ARG, "hidden and inter must be multiples of 32 and of group_size (a power of two >= 32)");
+  if (workspace_bytes < ks_b200_decode_layers_workspace(hidden, inter))
+    return fail(KS_ERR_WORKSPACE, "workspace smaller than ks_b200_decode_layers_workspace()");
+  int dev, rc;
+  if ((rc = current_device(&dev)) != KS_OK) return rc;
+  size_t off[kLayerRegions + 1];
+  layer_offsets(hidden, inter, off);
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  std::vector<DecodeLayerWeights> lw(n_layers);
+  for (size_t l = 0; l < n_layers; ++l) {
+    for (int k = 0; k < 5; ++k) {
+      lw[l].w[k] = weights[5 * l + k];
+      lw[l].s[k] = scales_f16[5 * l + k];
+    }
+    lw[l].norm1_w = norm1_w[l];
+    lw[l].norm2_w = norm2_w[l];
+  }
+  DecodeLayersArgs a{};
+  a.layers = (int)n_layers;
+  a.lw = lw.data();
+  a.h_in = h_in;
+  a.h_out = h_out;
+  const size_t hb = (hidden * 4 + 255) / 256 * 256;
+  a.hbuf[0] = reinterpret_cast<float *>(ws + off[kLayerRegions]);
+  a.hbuf[1] = reinterpret_cast<float *>(ws + off[kLayerRegions] + hb);
+  a.eps = eps;
+  a.hidden = (int64_t)hidden;
+  a.inter = (int64_t)inter;
+  a.group = (int64_t)group_size;
+  a.qkv = reinterpret_cast<float *>(ws + off[0]);
+  a.h2 = reinterpret_cast<float *>(ws + off[1]);
+  a.gate = reinterpret_cast<float *>(ws + off[2]);
+  a.up = reinterpret_cast<float *>(ws + off[3]);
+  a.act = reinterpret_cast<float *>(ws + off[4]);
+  a.scales = reinterpret_cast<float *>(ws + off[5]);
+  a.amax = reinterpret_cast<uint32_t *>(ws + off[6]);
+  for (int k = 0; k < 4; ++k) a.q[k] = reinterpret_cast<int8_t *>(ws + off[7 + k]);
+  a.status = status;
+  cudaError_t e = launch_decode_layers_w4a8(a, static_cast<cudaStream_t>(stream), dev);
+  if (e == cudaErrorInvalidValue)
+    return fail(KS_ERR_UNSUPPORTED, "decode layers need 16-byte aligned weights/scales and the streaming shape");
+  return e == cudaSuccess ? KS_OK : cuda_fail(e, "kernel launch");
+}
+
 extern "C" int ks_b200_decode_layer_launches(size_t hidden, size_t inter, size_t group_size) {
   if (hidden == 0 || inter == 0 || hidden % 32 || inter % 32 || group_size < 32 || group_size % 32 ||
       (group_size & (group_size - 1)) || hidden % group_size || inter % group_size)
@@ -1139,16 +1206,20 @@ extern "C" int ks_b200_decode_layer_launches(size_t hidden, size_t inter, size_t
   if (current_device(&dev) != KS_OK) return 0;
   // 16-byte aligned stand-ins: the dry run checks addresses, never reads them
   const auto *fake = reinterpret_cast<const uint8_t *>(uintptr_t(256));
-  DecodeLayerArgs a{};
-  a.h_in = a.norm1_w = a.norm2_w = reinterpret_cast<const float *>(fake);
+  DecodeLayerWeights lw{};
+  lw.norm1_w = lw.norm2_w = reinterpret_cast<const float *>(fake);
   for (int k = 0; k < 5; ++k) {
-    a.w[k] = fake;
-    a.s[k] = fake;
+    lw.w[k] = fake;
+    lw.s[k] = fake;
   }
+  DecodeLayersArgs a{};
+  a.layers = 1;
+  a.lw = &lw;
+  a.h_in = reinterpret_cast<const float *>(fake);
   a.hidden = (int64_t)hidden;
   a.inter = (int64_t)inter;
   a.group = (int64_t)group_size;
-  const cudaError_t e = launch_decode_layer_persistent(a, nullptr, dev, /*dry=*/true);
+  const cudaError_t e = launch_decode_layers_persistent(a, nullptr, dev, /*dry=*/true);
   cudaGetLastError();
   return e == cudaSuccess ? 1 : 4;
 }

@@ -1,5 +1,6 @@
-// ks_decode.cu -- the fused W4A8 decode layer (hidden h, intermediate i,
-// batch 1) as ONE persistent kernel on B200 (sm_100a).
+// ks_decode.cu -- fused W4A8 decode layers (hidden h, intermediate i,
+// batch 1) as ONE persistent kernel on B200 (sm_100a), up to 32 layers per
+// launch.  Per layer:
 //
 //   1  qkv   = W_qkv . q(RMSNorm(h_in, norm1))        [3h x h]
 //   2  h2    = h_in + W_o . q(qkv[2h:3h])             [h x h]   (attention at one position is V)
@@ -12,23 +13,30 @@
 // 32-element chunk, f16 group scales), so each stage's results are the same
 // as the four-launch path's for the same quantised input.
 //
-// Why one kernel: the layer is a chain of four dependent GEMVs whose weights
+// Why one kernel: a layer is a chain of four dependent GEMVs whose weights
 // (114 MB for h = 4096, i = 11008) are the whole cost.  Launched one by one,
 // each stage waits for the previous one to drain, then prepares its input,
 // and HBM idles in between.  Here a cooperative grid of one CTA per SM runs
-// all four stages:
-//   * warp 16 (producer) streams this CTA's rows of all five matrices, stage
-//     after stage, weights and f16 scale rows with cp.async.bulk (1-D, no
-//     tensor map, no multicast) into a ring of ~24 KB slots.  Weights do not
-//     depend on the activations, so it never waits for anything but a free
-//     slot and keeps HBM busy across the stage boundaries.
+// all four stages of every layer of the launch:
+//   * warp 16 (producer) streams this CTA's rows of all five matrices of
+//     every layer, stage after stage and layer after layer, weights and f16
+//     scale rows with cp.async.bulk (1-D, no tensor map, no multicast) into a
+//     ring of ~64 KB slots.  Weights do not depend on the activations, so it
+//     never waits for anything but a free slot and keeps HBM busy across the
+//     stage and layer boundaries (layer l + 1's QKV rows stream while layer
+//     l's down projection finishes).
 //   * warps 0-15 (consumers), per stage: wait at a grid barrier for the
 //     previous stage's outputs, prepare the input vector (RMSNorm /
 //     quantisation, identical in every CTA; each thread holds its 8-element
 //     groups in registers from one load to the quantised bytes), then take
 //     pairs of rows from the ring and write the stage's outputs with its
-//     epilogue.
-// The ring (~8 slots, ~195 KB per SM) holds about 4 us of HBM traffic.
+//     epilogue.  Between layers a fourth grid barrier hands the layer's
+//     output to the next layer's RMSNorm.
+// The ring (3 slots, ~195 KB per SM) holds about 4 us of HBM traffic.
+// Layer g of a call reads the previous layer's output and writes hbuf[g & 1]
+// (the last layer writes h_out); the intermediates (qkv, h2, gate, up, act)
+// are reused by every layer, each written after the barrier that ends the
+// previous layer's last read of it.
 //
 // Grid barrier: a 64-bit arrival counter in the workspace that only grows
 // (see grid_barrier); every spin is bounded (about one second) and on a
@@ -36,10 +44,12 @@
 // always terminates.  All CTAs are resident at once (cooperative launch), so
 // no CTA waits for one that cannot run.
 //
-// Within one launch no SM reads an activation address before another SM's
-// last write to it (each intermediate is written in one stage and read only
-// in later ones), so plain cached loads see the current data; max|act| is
-// updated with atomics in L2 and read with an L2 load.
+// Every read of an intermediate follows, through at least one grid barrier,
+// the write it must see (and every rewrite by a later layer follows the last
+// read of the previous value): the writers' CTA barrier and release
+// arrival, then the reader's acquire at GPU scope and CTA barrier, order
+// them for all threads of both CTAs, so plain loads see the current data;
+// max|act| is updated with atomics in L2 and read with an L2 load.
 
 #include <cuda_fp16.h>
 
@@ -59,15 +69,24 @@ constexpr int kDecCW = 16;  // consumer warps
 constexpr int kDecThreads = (kDecCW + 1) * 32;
 constexpr int kDecMaxSlots = 16;
 constexpr int kDecSlotTarget = 64 * 1024;  // bytes of one ring slot, about (fewer, longer copies)
+constexpr int kDecMaxLayers = 32;          // layers per launch (the parameter block holds their pointers)
 
-// One stage as both the producer and the consumers walk it.
+// One stage's shape as both the producer and the consumers walk it (the same
+// for every layer).  Matrix m of stage s is the layer's matrix kStageMat[s][m].
 struct DecStage {
-  const uint8_t *w[2];  // packed int4 rows, dense (row stride = row_bytes)
-  const uint8_t *s[2];  // f16 group-scale rows, dense (row stride = srow_bytes)
-  int32_t count;        // matrices (2: gate and up)
+  int32_t count;  // matrices (2: gate and up)
   int32_t rows, cols;
-  int32_t row_bytes, srow_bytes;
-  int32_t rps;  // rows per ring slot (even)
+  int32_t row_bytes, srow_bytes;  // dense rows: the row strides
+  int32_t rps;                    // rows per ring slot (even)
+};
+__constant__ int kStageMat[4][2] = {{0, 0}, {1, 1}, {2, 3}, {4, 4}};
+
+// One layer's operands: packed int4 weights and f16 scale rows of qkv, o,
+// gate, up, down; the RMSNorm weight vectors.
+struct DecLayer {
+  const uint8_t *w[5];
+  const uint8_t *s[5];
+  const float *norm1_w, *norm2_w;
 };
 
 struct DecParams {
@@ -75,17 +94,20 @@ struct DecParams {
   int32_t nslots, slot_bytes, xbuf_bytes;
   int32_t gshift;    // log2(group / 32)
   int32_t inflight;  // slots issued and not yet landed, at most (0: up to the ring)
-  int32_t l2_ahead;  // slots prefetched into L2 ahead of their copy
+  int32_t layers;        // layers in this launch
+  int32_t layer0;        // index of its first layer in the call
+  int32_t total_layers;  // layers in the call
   // activations and workspace
-  const float *h_in;
-  float *h_out;
-  const float *norm1_w, *norm2_w;
+  const float *h_in;  // input of the call's first layer
+  float *h_out;       // output of the call's last layer
+  float *hbuf[2];     // layer g (not the last) writes hbuf[g & 1]
   float eps;
   float *qkv, *h2, *gate, *up, *act, *scales;
   uint32_t *amax;
   unsigned long long *bar_count;  // 64-bit grid-barrier arrival counter
   int8_t *q[4];
   uint32_t *status;
+  DecLayer layer[kDecMaxLayers];
 };
 
 // ---- epilogues (Out types of W4A8Op::rows2) -------------------------------
@@ -127,13 +149,14 @@ struct SiluMulOut {
 
 // ---- grid barrier ----------------------------------------------------------
 // A 64-bit arrival counter in the workspace that only grows: every CTA adds 1
-// per barrier, kBarriers barriers per launch, so at the start of a launch it
-// holds kBarriers * grid * (launches so far) plus at most grid - 1 arrivals
-// of this launch; rounding down to a multiple of kBarriers * grid gives the
-// launch's base, and barrier k is passed once the counter reaches
-// base + (k + 1) * grid.  No reset, so the last arrival costs no extra round
-// trip.
-constexpr int kBarriers = 3;
+// per barrier and, after its last barrier, the arrivals of the barriers its
+// launch did not use, so every launch adds exactly kBarriers * grid.  At the
+// start of a launch the counter holds kBarriers * grid * (launches so far)
+// plus at most grid - 1 arrivals of this launch's first barrier; rounding
+// down to a multiple of kBarriers * grid gives the launch's base, and
+// barrier k is passed once the counter reaches base + (k + 1) * grid.  No
+// reset, so the last arrival costs no extra round trip.
+constexpr int kBarriers = 4 * kDecMaxLayers;
 
 __device__ __forceinline__ uint64_t ld_acquire_gpu_u64(const unsigned long long *p) {
   uint64_t v;
@@ -147,16 +170,17 @@ __device__ __forceinline__ uint64_t barrier_base(const unsigned long long *count
   return v - v % per_launch;
 }
 
-// Every consumer thread of every CTA calls it, k = 0, 1, 2 in order.  All of
+// Every consumer thread of every CTA calls it, k = 0, 1, 2, ... in order.  All of
 // this CTA's consumer writes before it are visible to every consumer thread
 // of the grid after it.
-__device__ void grid_barrier(unsigned long long *count, uint64_t base, int k, int ctid, uint32_t *status) {
+// base: the launch's barrier base, in shared memory (read by thread 0 only).
+__device__ void grid_barrier(unsigned long long *count, const uint64_t *base, int k, int ctid, uint32_t *status) {
   consumers_sync<kDecCW>();
   if (ctid == 0) {
     // release: this CTA's writes (ordered before it by the CTA barrier) are
     // visible to whoever acquires a count that includes this arrival
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(count) : "memory");
-    const uint64_t target = base + (uint64_t)(k + 1) * gridDim.x;
+    const uint64_t target = *base + (uint64_t)(k + 1) * gridDim.x;
     const uint64_t t0 = globaltimer_ns();
     while ((int64_t)(ld_acquire_gpu_u64(count) - target) < 0) {
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -323,6 +347,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   uint64_t *empty = full + P.nslots;
   float *red = reinterpret_cast<float *>(smem + kBarBytes - 128);  // kDecCW floats
   uint32_t *amax_cta = reinterpret_cast<uint32_t *>(smem + kBarBytes - 192);  // this CTA's max|act| bits
+  uint64_t *bar_base = reinterpret_cast<uint64_t *>(smem + kBarBytes - 256);  // the launch's barrier base
   uint8_t *xb = smem + kBarBytes;
   uint8_t *ring = xb + P.xbuf_bytes;
 
@@ -342,68 +367,43 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      // L2 prefetch cursor, l2_ahead slots ahead of the copies: while the
-      // consumers sit at a grid barrier and the ring is full, HBM keeps
-      // streaming the next slots into L2, and their copies then come from L2.
-      int cs = 0, cm = 0, clo = 0, cn = 0;
-      int64_t cr0 = 0;
-      rows_of(P.st[0], cr0, cn);
-      auto settle = [&]() {
-        while (cs < 4 && clo >= cn) {
-          clo = 0;
-          if (++cm >= P.st[cs].count) {
-            cm = 0;
-            if (++cs < 4) rows_of(P.st[cs], cr0, cn);
-          }
-        }
-      };
-      auto advance = [&]() {
-        clo += P.st[cs].rps;
-        settle();
-      };
-      auto prefetch = [&]() {
-        const DecStage &S = P.st[cs];
-        const uint32_t n = (uint32_t)min(S.rps, cn - clo);
-        bulk_prefetch_l2(S.w[cm] + (cr0 + clo) * S.row_bytes, n * (uint32_t)S.row_bytes);
-        bulk_prefetch_l2(S.s[cm] + (cr0 + clo) * S.srow_bytes, n * (uint32_t)S.srow_bytes);
-        advance();
-      };
-      settle();
-      for (int j = 0; j < P.nslots && cs < 4; ++j) advance();
-      for (int j = 0; j < P.l2_ahead && cs < 4; ++j) prefetch();
       int gs = 0;
       bool stop = false;
-      for (int s = 0; s < 4 && !stop; ++s) {
-        const DecStage &S = P.st[s];
-        int64_t r0;
-        int rows_cta;
-        rows_of(S, r0, rows_cta);
-        for (int m = 0; m < S.count && !stop; ++m) {
-          for (int lo = 0; lo < rows_cta; lo += S.rps, ++gs) {
-            const int b = gs % P.nslots;
-            if (gs >= P.nslots && !mbar_wait(&empty[b], (uint32_t)((gs / P.nslots) - 1) & 1u)) {
-              set_status(P.status, kStatusTimeout);
-              stop = true;
-              break;
-            }
-            // at most `inflight` slots issued and not yet landed: a shorter
-            // memory queue keeps the barrier's and the input loads' latency low
-            if (P.inflight > 0 && gs >= P.inflight) {
-              const int g2 = gs - P.inflight;
-              if (!mbar_wait(&full[g2 % P.nslots], (uint32_t)(g2 / P.nslots) & 1u)) {
+      for (int l = 0; l < P.layers && !stop; ++l) {
+        const DecLayer &Ly = P.layer[l];
+        for (int s = 0; s < 4 && !stop; ++s) {
+          const DecStage &S = P.st[s];
+          int64_t r0;
+          int rows_cta;
+          rows_of(S, r0, rows_cta);
+          for (int m = 0; m < S.count && !stop; ++m) {
+            const uint8_t *wm = Ly.w[kStageMat[s][m]];
+            const uint8_t *sm = Ly.s[kStageMat[s][m]];
+            for (int lo = 0; lo < rows_cta; lo += S.rps, ++gs) {
+              const int b = gs % P.nslots;
+              if (gs >= P.nslots && !mbar_wait(&empty[b], (uint32_t)((gs / P.nslots) - 1) & 1u)) {
                 set_status(P.status, kStatusTimeout);
                 stop = true;
                 break;
               }
+              // at most `inflight` slots issued and not yet landed: a shorter
+              // memory queue keeps the barrier's and the input loads' latency low
+              if (P.inflight > 0 && gs >= P.inflight) {
+                const int g2 = gs - P.inflight;
+                if (!mbar_wait(&full[g2 % P.nslots], (uint32_t)(g2 / P.nslots) & 1u)) {
+                  set_status(P.status, kStatusTimeout);
+                  stop = true;
+                  break;
+                }
+              }
+              const int n = min(S.rps, rows_cta - lo);
+              const uint32_t wbytes = (uint32_t)n * (uint32_t)S.row_bytes;
+              const uint32_t sbytes = (uint32_t)n * (uint32_t)S.srow_bytes;
+              uint8_t *dst = ring + (size_t)b * P.slot_bytes;
+              mbar_arrive_expect_tx(&full[b], wbytes + sbytes);
+              bulk_g2s_hint(dst, wm + (r0 + lo) * S.row_bytes, wbytes, &full[b], pol);
+              bulk_g2s(dst + (size_t)S.rps * S.row_bytes, sm + (r0 + lo) * S.srow_bytes, sbytes, &full[b]);
             }
-            const int n = min(S.rps, rows_cta - lo);
-            const uint32_t wbytes = (uint32_t)n * (uint32_t)S.row_bytes;
-            const uint32_t sbytes = (uint32_t)n * (uint32_t)S.srow_bytes;
-            uint8_t *dst = ring + (size_t)b * P.slot_bytes;
-            mbar_arrive_expect_tx(&full[b], wbytes + sbytes);
-            bulk_g2s_hint(dst, S.w[m] + (r0 + lo) * S.row_bytes, wbytes, &full[b], pol);
-            bulk_g2s(dst + (size_t)S.rps * S.row_bytes, S.s[m] + (r0 + lo) * S.srow_bytes, sbytes, &full[b]);
-            if (gs >= P.nslots && P.l2_ahead > 0 && cs < 4) prefetch();
           }
         }
       }
@@ -418,67 +418,91 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   constexpr int JH = NH / 4, JI = NI / 4;  // 8-element groups per thread (NT = 512)
   const int ctid = threadIdx.x;
   const int64_t h = P.st[1].rows, inter = P.st[2].rows;
-  int gs = 0, pair_base = 0;
+  int gs = 0, pair_base = 0, bk = 0;
   uint32_t mx = 0;
   bool stop = false;
   int64_t r0;
   int nr;
-  const uint64_t base = ctid == 0 ? barrier_base(P.bar_count) : 0;
-  // RMSNorm weights of this thread's groups, for stages 1 and 3, loaded once
-  float n1[JH][8], n2[JH][8];
-  load_groups<JH>(P.norm1_w, (int)(h / 8), ctid, n1);
-  load_groups<JH>(P.norm2_w, (int)(h / 8), ctid, n2);
+  if (ctid == 0) *bar_base = barrier_base(P.bar_count);
+  // RMSNorm weights of this thread's groups for the next RMSNorm (stage 1
+  // or 3): each vector is loaded before the grid barrier that precedes its
+  // stage, since it does not depend on it, and only one is held at a time
+  float nw[JH][8];
+  load_groups<JH>(P.layer[0].norm1_w, (int)(h / 8), ctid, nw);
 
-  // stage 1: qkv = W_qkv . q(RMSNorm(h_in, norm1))
-  if (blockIdx.x == 0 && ctid == 0) atomicExch(P.amax, 0u);
-  {
-    float v[JH][8];
-    load_groups<JH>(P.h_in, (int)(h / 8), ctid, v);
-    prep_groups<JH>((int)h, kPrepRms, v, n1, P.eps, 0.0f, xb, P.q[0], P.scales + 0, red, ctid);
-    rows_of(P.st[0], r0, nr);
-    consume_matrix<NH>(P, P.st[0], PlainOut{P.qkv}, xb, ring, full, empty, r0, nr, gs, pair_base, mx, stop, warp,
-                       lane);
-  }
-  grid_barrier(P.bar_count, base, 0, ctid, P.status);
+  for (int l = 0; l < P.layers; ++l) {
+    // this layer's input and output vectors, computed where used (fewer live registers)
+    auto h_in = [&]() -> const float * {
+      const int g = P.layer0 + l;
+      return g == 0 ? P.h_in : P.hbuf[(g - 1) & 1];
+    };
+    auto h_out = [&]() -> float * {
+      const int g = P.layer0 + l;
+      return g == P.total_layers - 1 ? P.h_out : P.hbuf[g & 1];
+    };
+    // stage 1: qkv = W_qkv . q(RMSNorm(h_in, norm1))
+    if (blockIdx.x == 0 && ctid == 0) atomicExch(P.amax, 0u);
+    {
+      float v[JH][8];
+      load_groups<JH>(h_in(), (int)(h / 8), ctid, v);
+      prep_groups<JH>((int)h, kPrepRms, v, nw, P.eps, 0.0f, xb, P.q[0], P.scales + 0, red, ctid);
+      rows_of(P.st[0], r0, nr);
+      consume_matrix<NH>(P, P.st[0], PlainOut{P.qkv}, xb, ring, full, empty, r0, nr, gs, pair_base, mx, stop, warp,
+                         lane);
+    }
+    grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
 
-  // stage 2: h2 = h_in + W_o . q(qkv[2h:3h])
-  {
-    float v[JH][8];
-    load_groups<JH>(P.qkv + 2 * h, (int)(h / 8), ctid, v);
-    prep_groups<JH>((int)h, kPrepPlain, v, n1, P.eps, 0.0f, xb, P.q[1], P.scales + 1, red, ctid);
-    rows_of(P.st[1], r0, nr);
-    consume_matrix<NH>(P, P.st[1], ResidualOut{P.h2, P.h_in}, xb, ring, full, empty, r0, nr, gs, pair_base, mx,
-                       stop, warp, lane);
-  }
-  grid_barrier(P.bar_count, base, 1, ctid, P.status);
+    // stage 2: h2 = h_in + W_o . q(qkv[2h:3h])
+    {
+      float v[JH][8];
+      load_groups<JH>(P.qkv + 2 * h, (int)(h / 8), ctid, v);
+      prep_groups<JH>((int)h, kPrepPlain, v, nw, P.eps, 0.0f, xb, P.q[1], P.scales + 1, red, ctid);
+      rows_of(P.st[1], r0, nr);
+      consume_matrix<NH>(P, P.st[1], ResidualOut{P.h2, h_in()}, xb, ring, full, empty, r0, nr, gs, pair_base, mx,
+                         stop, warp, lane);
+    }
+    load_groups<JH>(P.layer[l].norm2_w, (int)(h / 8), ctid, nw);
+    grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
 
-  // stage 3: gate, up = W_g, W_u . q(RMSNorm(h2, norm2)); act = silu(gate) * up
-  {
-    float v[JH][8];
-    load_groups<JH>(P.h2, (int)(h / 8), ctid, v);
-    prep_groups<JH>((int)h, kPrepRms, v, n2, P.eps, 0.0f, xb, P.q[2], P.scales + 2, red, ctid);
-    rows_of(P.st[2], r0, nr);
-    consume_matrix<NH>(P, P.st[2], PlainOut{P.gate}, xb, ring, full, empty, r0, nr, gs, pair_base, mx, stop, warp,
-                       lane);
-    consumers_sync<kDecCW>();  // gate rows (any warp) before the up pass reads them
-    consume_matrix<NH>(P, P.st[2], SiluMulOut{P.up, P.gate, P.act, amax_cta}, xb, ring, full, empty, r0, nr, gs,
-                       pair_base, mx, stop, warp, lane);
-    consumers_sync<kDecCW>();
-    if (ctid == 0) atomicMax(P.amax, *amax_cta);
-  }
-  grid_barrier(P.bar_count, base, 2, ctid, P.status);
+    // stage 3: gate, up = W_g, W_u . q(RMSNorm(h2, norm2)); act = silu(gate) * up
+    {
+      float v[JH][8];
+      load_groups<JH>(P.h2, (int)(h / 8), ctid, v);
+      prep_groups<JH>((int)h, kPrepRms, v, nw, P.eps, 0.0f, xb, P.q[2], P.scales + 2, red, ctid);
+      rows_of(P.st[2], r0, nr);
+      consume_matrix<NH>(P, P.st[2], PlainOut{P.gate}, xb, ring, full, empty, r0, nr, gs, pair_base, mx, stop,
+                         warp, lane);
+      consumers_sync<kDecCW>();  // gate rows (any warp) before the up pass reads them
+      consume_matrix<NH>(P, P.st[2], SiluMulOut{P.up, P.gate, P.act, amax_cta}, xb, ring, full, empty, r0, nr, gs,
+                         pair_base, mx, stop, warp, lane);
+      consumers_sync<kDecCW>();
+      if (ctid == 0) {
+        atomicMax(P.amax, *amax_cta);
+        *amax_cta = 0u;  // the next layer's stage 3 starts from zero
+      }
+    }
+    grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
 
-  // stage 4: h_out = h2 + W_d . q(act), scale from max|act| (atomics, read from L2)
-  {
-    float v[JI][8];
-    const float amax = __uint_as_float(__ldcg(P.amax));
-    load_groups<JI>(P.act, (int)(inter / 8), ctid, v);
-    float unused[JI][8] = {};
-    prep_groups<JI>((int)inter, kPrepAmaxGiven, v, unused, P.eps, amax, xb, P.q[3], P.scales + 3, red, ctid);
-    rows_of(P.st[3], r0, nr);
-    consume_matrix<NI>(P, P.st[3], ResidualOut{P.h_out, P.h2}, xb, ring, full, empty, r0, nr, gs, pair_base, mx,
-                       stop, warp, lane);
+    // stage 4: h_out = h2 + W_d . q(act), scale from max|act| (atomics, read from L2)
+    {
+      float v[JI][8];
+      const float amax = __uint_as_float(__ldcg(P.amax));
+      load_groups<JI>(P.act, (int)(inter / 8), ctid, v);
+      float unused[JI][8] = {};
+      prep_groups<JI>((int)inter, kPrepAmaxGiven, v, unused, P.eps, amax, xb, P.q[3], P.scales + 3, red, ctid);
+      rows_of(P.st[3], r0, nr);
+      consume_matrix<NI>(P, P.st[3], ResidualOut{h_out(), P.h2}, xb, ring, full, empty, r0, nr, gs, pair_base, mx,
+                         stop, warp, lane);
+    }
+    if (l + 1 < P.layers) {
+      load_groups<JH>(P.layer[l + 1].norm1_w, (int)(h / 8), ctid, nw);
+      grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);  // h_out before the next layer's RMSNorm
+    }
   }
+  // every launch adds kBarriers arrivals per CTA: the ones this launch did not use
+  if (ctid == 0 && bk < kBarriers)
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(P.bar_count), "l"((uint64_t)(kBarriers - bk))
+                 : "memory");
   if (__any_sync(0xffffffffu, W4A8Op<__half, NH, false>::bad(mx)) && lane == 0) set_status(P.status, kStatusBadScale);
 }
 
@@ -523,15 +547,16 @@ cudaError_t launch_persistent(const DecParams &P, size_t smem, cudaStream_t stre
 
 }  // namespace
 
-cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device, bool dry) {
+cudaError_t launch_decode_layers_persistent(const DecodeLayersArgs &a, cudaStream_t stream, int device, bool dry) {
   if (env_int("KS_B200_DECODE_PERSISTENT", 1) == 0) return cudaErrorNotSupported;
+  if (a.layers < 1) return cudaErrorInvalidValue;
   const int64_t h = a.hidden, i = a.inter, G = a.group;
   const int NH = ncpl_for(h), NI = ncpl_for(i);
   if (!((NH == 4 && (NI == 12 || NI == 16)) || (NH == 8 && NI == 16))) return cudaErrorNotSupported;
   DecParams P{};
   const int64_t rows[4] = {3 * h, h, i, h}, cols[4] = {h, h, h, i};
   const int counts[4] = {1, 1, 2, 1};
-  const int widx[4][2] = {{0, 0}, {1, 1}, {2, 3}, {4, 4}};
+  const int target = std::max(8, env_int("KS_B200_DECODE_SLOT_KB", kDecSlotTarget / 1024)) * 1024;
   int slot = 0, xbuf = 0;
   for (int s = 0; s < 4; ++s) {
     DecStage &S = P.st[s];
@@ -541,21 +566,19 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
     S.row_bytes = (int32_t)(cols[s] / 2);
     S.srow_bytes = (int32_t)(cols[s] / G * 2);
     if (S.row_bytes % 16 || S.srow_bytes % 16) return cudaErrorNotSupported;  // bulk-copy granularity
-    for (int m = 0; m < 2; ++m) {
-      S.w[m] = a.w[widx[s][m]];
-      S.s[m] = static_cast<const uint8_t *>(a.s[widx[s][m]]);
-      if ((reinterpret_cast<uintptr_t>(S.w[m]) | reinterpret_cast<uintptr_t>(S.s[m])) & 15u)
-        return cudaErrorNotSupported;
-    }
     const int rt = S.row_bytes + S.srow_bytes;
-    const int target = std::max(8, env_int("KS_B200_DECODE_SLOT_KB", kDecSlotTarget / 1024)) * 1024;
     S.rps = std::max(2, (target / rt) & ~1);
     slot = std::max(slot, S.rps * rt);
     xbuf = std::max(xbuf, W4A8Op<__half, 4, false>::xbuf_bytes((int)(cols[s] / 32)));
   }
-  if ((reinterpret_cast<uintptr_t>(a.h_in) | reinterpret_cast<uintptr_t>(a.norm1_w) |
-       reinterpret_cast<uintptr_t>(a.norm2_w)) & 15u)
-    return cudaErrorNotSupported;  // 16-byte vector loads of the inputs
+  // 16-byte vector loads of the inputs, 16-byte bulk copies of the weights
+  uintptr_t al = reinterpret_cast<uintptr_t>(a.h_in);
+  for (int l = 0; l < a.layers; ++l) {
+    const DecodeLayerWeights &lw = a.lw[l];
+    al |= reinterpret_cast<uintptr_t>(lw.norm1_w) | reinterpret_cast<uintptr_t>(lw.norm2_w);
+    for (int k = 0; k < 5; ++k) al |= reinterpret_cast<uintptr_t>(lw.w[k]) | reinterpret_cast<uintptr_t>(lw.s[k]);
+  }
+  if (al & 15u) return cudaErrorNotSupported;
   slot = (slot + 127) / 128 * 128;
   const DeviceProps &dp = device_props(device);
   const int nslots = std::min(kDecMaxSlots, (dp.smem_optin - kBarBytes - xbuf) / slot);
@@ -567,13 +590,11 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
   while ((int64_t(32) << gshift) < G) ++gshift;
   P.gshift = gshift;
   P.inflight = std::max(0, std::min(env_int("KS_B200_DECODE_INFLIGHT", 0), nslots - 1));
-  // off by default: measured slower (the prefetches queue ahead of the
-  // grid barrier's and the input vector's latency-bound accesses)
-  P.l2_ahead = std::max(0, env_int("KS_B200_DECODE_L2_AHEAD", 0));
+  P.total_layers = a.layers;
   P.h_in = a.h_in;
   P.h_out = a.h_out;
-  P.norm1_w = a.norm1_w;
-  P.norm2_w = a.norm2_w;
+  P.hbuf[0] = a.hbuf[0];
+  P.hbuf[1] = a.hbuf[1];
   P.eps = a.eps;
   P.qkv = a.qkv;
   P.h2 = a.h2;
@@ -586,9 +607,65 @@ cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_
   for (int k = 0; k < 4; ++k) P.q[k] = a.q[k];
   P.status = a.status;
   const size_t smem = (size_t)kBarBytes + xbuf + (size_t)nslots * slot;
-  if (NH == 4 && NI == 12) return launch_persistent<4, 12>(P, smem, stream, device, dry);
-  if (NH == 4 && NI == 16) return launch_persistent<4, 16>(P, smem, stream, device, dry);
-  return launch_persistent<8, 16>(P, smem, stream, device, dry);
+  for (int l0 = 0; l0 < a.layers; l0 += kDecMaxLayers) {
+    P.layer0 = l0;
+    P.layers = std::min(kDecMaxLayers, a.layers - l0);
+    for (int l = 0; l < P.layers; ++l) {
+      const DecodeLayerWeights &lw = a.lw[l0 + l];
+      for (int k = 0; k < 5; ++k) {
+        P.layer[l].w[k] = lw.w[k];
+        P.layer[l].s[k] = static_cast<const uint8_t *>(lw.s[k]);
+      }
+      P.layer[l].norm1_w = lw.norm1_w;
+      P.layer[l].norm2_w = lw.norm2_w;
+    }
+    cudaError_t e;
+    if (NH == 4 && NI == 12)
+      e = launch_persistent<4, 12>(P, smem, stream, device, dry);
+    else if (NH == 4 && NI == 16)
+      e = launch_persistent<4, 16>(P, smem, stream, device, dry);
+    else
+      e = launch_persistent<8, 16>(P, smem, stream, device, dry);
+    if (e != cudaSuccess || dry) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_decode_layers_w4a8(const DecodeLayersArgs &a, cudaStream_t stream, int device) {
+  {
+    const cudaError_t e = launch_decode_layers_persistent(a, stream, device);
+    if (e == cudaSuccess) return e;
+    if (e != cudaErrorNotSupported && e != cudaErrorCooperativeLaunchTooLarge) return e;
+    cudaGetLastError();  // not a sticky error: take four launches per layer below
+  }
+  for (int l = 0; l < a.layers; ++l) {
+    const DecodeLayerWeights &lw = a.lw[l];
+    DecodeLayerArgs d{};
+    d.h_in = l == 0 ? a.h_in : a.hbuf[(l - 1) & 1];
+    d.h_out = l == a.layers - 1 ? a.h_out : a.hbuf[l & 1];
+    d.norm1_w = lw.norm1_w;
+    d.norm2_w = lw.norm2_w;
+    d.eps = a.eps;
+    for (int k = 0; k < 5; ++k) {
+      d.w[k] = lw.w[k];
+      d.s[k] = lw.s[k];
+    }
+    d.hidden = a.hidden;
+    d.inter = a.inter;
+    d.group = a.group;
+    d.qkv = a.qkv;
+    d.h2 = a.h2;
+    d.gate = a.gate;
+    d.up = a.up;
+    d.act = a.act;
+    d.scales = a.scales;
+    d.amax = a.amax;
+    for (int k = 0; k < 4; ++k) d.q[k] = a.q[k];
+    d.status = a.status;
+    const cudaError_t e = launch_decode_layer_four(d, stream, device);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace ksb

@@ -864,12 +864,35 @@ cudaError_t launch_peer_wait(const uint32_t *counters, int ncounters, uint32_t *
 //   3  gate = W_g . q(RMSNorm(h2, norm2)), up = W_u . (same); act = silu(gate) * up, max|act|
 //   4  h_out = h2 + W_d . q(act)                          (scale from max|act|)
 cudaError_t launch_decode_layer_w4a8(const DecodeLayerArgs &a, cudaStream_t stream, int device) {
-  {
-    const cudaError_t e = launch_decode_layer_persistent(a, stream, device);
-    if (e == cudaSuccess) return e;
-    if (e != cudaErrorNotSupported && e != cudaErrorCooperativeLaunchTooLarge) return e;
-    cudaGetLastError();  // not a sticky error: take the four launches below
+  DecodeLayerWeights lw{};
+  for (int k = 0; k < 5; ++k) {
+    lw.w[k] = a.w[k];
+    lw.s[k] = a.s[k];
   }
+  lw.norm1_w = a.norm1_w;
+  lw.norm2_w = a.norm2_w;
+  DecodeLayersArgs c{};
+  c.layers = 1;
+  c.lw = &lw;
+  c.h_in = a.h_in;
+  c.h_out = a.h_out;
+  c.eps = a.eps;
+  c.hidden = a.hidden;
+  c.inter = a.inter;
+  c.group = a.group;
+  c.qkv = a.qkv;
+  c.h2 = a.h2;
+  c.gate = a.gate;
+  c.up = a.up;
+  c.act = a.act;
+  c.scales = a.scales;
+  c.amax = a.amax;
+  for (int k = 0; k < 4; ++k) c.q[k] = a.q[k];
+  c.status = a.status;
+  return launch_decode_layers_w4a8(c, stream, device);
+}
+
+cudaError_t launch_decode_layer_four(const DecodeLayerArgs &a, cudaStream_t stream, int device) {
   const int64_t h = a.hidden, i = a.inter;
   struct Stage {
     int64_t rows, cols;

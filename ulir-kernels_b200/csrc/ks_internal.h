@@ -131,12 +131,41 @@ struct DecodeLayerArgs {
   uint32_t *status;
 };
 cudaError_t launch_decode_layer_w4a8(const DecodeLayerArgs &a, cudaStream_t stream, int device);
-// The same layer as one cooperative persistent kernel; cudaErrorNotSupported
-// when the shape, the alignment or the device does not allow it (the caller
-// then uses the four-launch path).
+// The same layer as four chained GEMV launches (the fallback of the
+// persistent kernel).
+cudaError_t launch_decode_layer_four(const DecodeLayerArgs &a, cudaStream_t stream, int device);
+
+// A chain of decode layers: layer g reads the previous layer's output and
+// writes its own, h_in -> hbuf[0] -> hbuf[1] -> hbuf[0] ... -> h_out (layer g
+// writes hbuf[g & 1] unless it is the last).  Per layer: the five weight
+// matrices (qkv, o, gate, up, down) with f16 scales, and the two RMSNorm
+// weight vectors.  The workspace regions are those of DecodeLayerArgs,
+// reused by every layer.
+struct DecodeLayerWeights {
+  const uint8_t *w[5];
+  const void *s[5];
+  const float *norm1_w, *norm2_w;
+};
+struct DecodeLayersArgs {
+  int layers;
+  const DecodeLayerWeights *lw;  // host array of `layers` entries
+  const float *h_in;
+  float *h_out;
+  float *hbuf[2];
+  float eps;
+  int64_t hidden, inter, group;
+  float *qkv, *h2, *gate, *up, *act, *scales;
+  uint32_t *amax;
+  int8_t *q[4];
+  uint32_t *status;
+};
+cudaError_t launch_decode_layers_w4a8(const DecodeLayersArgs &a, cudaStream_t stream, int device);
+// The chain as cooperative persistent launches of up to 32 layers each;
+// cudaErrorNotSupported when the shape, the alignment or the device does not
+// allow it (the caller then uses four launches per layer).
 // dry: every check (shape, alignment, occupancy), no launch
-cudaError_t launch_decode_layer_persistent(const DecodeLayerArgs &a, cudaStream_t stream, int device,
-                                           bool dry = false);
+cudaError_t launch_decode_layers_persistent(const DecodeLayersArgs &a, cudaStream_t stream, int device,
+                                            bool dry = false);
 
 // Wait (bounded by limit_ns) until each of counters[0 .. ncounters) reaches
 // expected[0] + arrivals; expected[0] then holds the new target.

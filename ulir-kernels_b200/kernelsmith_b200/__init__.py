@@ -101,6 +101,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ks_b200_peer_arrival_wait_ranks_async": (c_int, [_vp, c_int, _vp, c_uint32, ctypes.c_uint64, _vp, _vp]),
     "ks_b200_status_check": (c_int, [_vp, _vp]),
     "ks_b200_decode_layer_workspace": (_sz, [_sz, _sz]),
+    "ks_b200_decode_layers_workspace": (_sz, [_sz, _sz]),
+    "ks_b200_decode_layers_w4a8_async": (
+        c_int,
+        [_sz, _vp, _vp, _vp, _vp, _f, _vp, _vp, _sz, _sz, _sz, _vp, _sz, _vp, _vp],
+    ),
     "ks_b200_decode_layer_offsets": (c_int, [_sz, _sz, _vp]),
     "ks_b200_decode_layer_w4a8_async": (
         c_int,
