@@ -224,12 +224,15 @@ __device__ __forceinline__ void load_groups(const float *x, int ngroups, int cti
 
 enum PrepMode { kPrepPlain, kPrepRms, kPrepAmaxGiven };
 
-// v: the thread's groups (loaded); nw: RMSNorm weights of the same groups.
-template <int J>
-__device__ void prep_groups(int K, int mode, float (&v)[J][8], const float (&nw)[J][8], float eps, float amax_given,
-                            uint8_t *xb, int8_t *xq_out, float *xs_out, float *red, int ctid) {
+// v: the thread's groups (loaded); nw: RMSNorm weights of the same groups
+// (read only in kPrepRms mode).
+template <int J, int MODE, int JW>
+__device__ __forceinline__ void prep_groups(int K, float (&v)[J][8], const float (&nw)[JW][8], float eps,
+                                            float amax_given, uint8_t *xb, int8_t *xq_out, float *xs_out, float *red,
+                                            int ctid) {
+  static_assert(MODE != kPrepRms || JW == J, "RMSNorm weights for every group");
   const int ngroups = K / 8, chunks = K / 32;
-  if (mode == kPrepRms) {
+  if constexpr (MODE == kPrepRms) {
     float ss = 0.0f;
 #pragma unroll
     for (int j = 0; j < J; ++j)
@@ -243,7 +246,7 @@ __device__ void prep_groups(int K, int mode, float (&v)[J][8], const float (&nw)
       for (int t = 0; t < 8; ++t) v[j][t] = __fmul_rn(__fmul_rn(v[j][t], scale), nw[j][t]);
   }
   float amax;
-  if (mode == kPrepAmaxGiven) {
+  if constexpr (MODE == kPrepAmaxGiven) {
     amax = amax_given;
   } else {
     float m = 0.0f;
@@ -294,49 +297,60 @@ __device__ void prep_groups(int K, int mode, float (&v)[J][8], const float (&nw)
   consumers_sync<kDecCW>();
 }
 
+// ---- ring position, kept incrementally (no division per slot) --------------
+struct RingPos {
+  int b = 0;           // slot
+  uint32_t phase = 0;  // parity of the slot's current use
+  __device__ __forceinline__ void next(int nslots) {
+    if (++b == nslots) {
+      b = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// This CTA's rows of one stage, computed once per launch (shared memory):
+// a contiguous block balanced to one row, and its ring slots.
+struct StageRows {
+  int r0, n, nblk;
+};
+
 // ---- consumers: one matrix of one stage -------------------------------------
 template <int NCPL, class Out>
-__device__ __forceinline__ void consume_matrix(const DecParams &P, const DecStage &S, const Out &out,
-                                               const uint8_t *xb, const uint8_t *ring, uint64_t *full,
-                                               uint64_t *empty, int64_t r0, int rows_cta, int &gs, int &pair_base,
-                                               uint32_t &mx, bool &stop, int warp, int lane) {
+__device__ __forceinline__ void consume_matrix(const DecStage &S, const StageRows &G, const Out &out,
+                                               const uint8_t *xb, int gshift, const uint8_t *ring, int slot_bytes,
+                                               int nslots, uint64_t *full, uint64_t *empty, RingPos &rp,
+                                               int &pair_base, uint32_t &mx, bool &stop, int warp, int lane,
+                                               uint32_t *status) {
   using Op = W4A8Op<__half, NCPL, false>;
-  const W4A8OpParams op{S.cols / 32, P.gshift, 1.0f, 0, 0};
+  const W4A8OpParams op{S.cols / 32, gshift, 1.0f, 0, 0};
   typename Op::Lane L;
   Op::lane_init(op, L, xb, lane);
   const GemvItem none{};
-  const int nblk = (rows_cta + S.rps - 1) / S.rps;
-  for (int st = 0; st < nblk; ++st, ++gs) {
-    if (stop) continue;  // keeps gs in step with the producer's numbering
-    const int b = gs % P.nslots;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[b], (uint32_t)(gs / P.nslots) & 1u));
+  for (int st = 0, lo = 0; st < G.nblk; ++st, lo += S.rps, rp.next(nslots)) {
+    if (stop) continue;  // keeps the ring position in step with the producer
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[rp.b], rp.phase));
     if (!ok) {
-      if (lane == 0) set_status(P.status, kStatusTimeout);
+      if (lane == 0) set_status(status, kStatusTimeout);
       stop = true;
       continue;
     }
-    const int lo = st * S.rps;
-    const int hi = min(lo + S.rps, rows_cta);
-    const uint8_t *base = ring + (size_t)b * P.slot_bytes;
+    const int hi = min(lo + S.rps, G.n);
+    const uint8_t *base = ring + (size_t)rp.b * slot_bytes;
     const uint8_t *sbase = base + (size_t)S.rps * S.row_bytes;
     // row pairs (lo + 2q, lo + 2q + 1); the pair's running index picks the
     // warp, so consecutive slots start on different warps
-    const int pair0 = pair_base + lo / 2;
-    for (int q = ((warp - pair0 % kDecCW) + kDecCW) % kDecCW; lo + 2 * q < hi; q += kDecCW) {
+    const int pair0 = pair_base + (lo >> 1);  // rps is even
+    for (int q = (warp - pair0) & (kDecCW - 1); lo + 2 * q < hi; q += kDecCW) {
       const int li = 2 * q;
       mx = max(mx, Op::rows2(op, L, xb, base + (size_t)li * S.row_bytes, sbase + (size_t)li * S.srow_bytes,
                              base + (size_t)(li + 1) * S.row_bytes, sbase + (size_t)(li + 1) * S.srow_bytes, out,
-                             none, r0 + lo + li, lo + li + 1 < hi, lane, L));
+                             none, (int64_t)G.r0 + lo + li, lo + li + 1 < hi, lane, L));
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[b]);
+    if (lane == 0) mbar_arrive(&empty[rp.b]);
   }
-  pair_base += (rows_cta + 1) / 2;
-}
-
-__device__ __forceinline__ void rows_of(const DecStage &S, int64_t &r0, int &n) {
-  r0 = (int64_t)blockIdx.x * S.rows / gridDim.x;
-  n = (int)((int64_t)(blockIdx.x + 1) * S.rows / gridDim.x - r0);
+  pair_base += (G.n + 1) >> 1;
 }
 
 // NH, NI: 32-element chunks per lane for rows of h and of i columns.
@@ -348,6 +362,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   float *red = reinterpret_cast<float *>(smem + kBarBytes - 128);  // kDecCW floats
   uint32_t *amax_cta = reinterpret_cast<uint32_t *>(smem + kBarBytes - 192);  // this CTA's max|act| bits
   uint64_t *bar_base = reinterpret_cast<uint64_t *>(smem + kBarBytes - 256);  // the launch's barrier base
+  StageRows *geo = reinterpret_cast<StageRows *>(smem + kBarBytes - 512);  // 4 stages
   uint8_t *xb = smem + kBarBytes;
   uint8_t *ring = xb + P.xbuf_bytes;
 
@@ -358,6 +373,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
       mbar_init(&full[b], 1);
       mbar_init(&empty[b], kDecCW);
     }
+    for (int s = 0; s < 4; ++s) {
+      const DecStage &S = P.st[s];
+      const int r0 = (int)((int64_t)blockIdx.x * S.rows / gridDim.x);
+      const int r1 = (int)((int64_t)(blockIdx.x + 1) * S.rows / gridDim.x);
+      geo[s] = StageRows{r0, r1 - r0, (r1 - r0 + S.rps - 1) / S.rps};
+    }
     *amax_cta = 0u;
     fence_mbarrier_init();
   }
@@ -367,49 +388,49 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
     // ------------------------------------------------------------ producer --
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      int gs = 0;
+      RingPos rp, landed;  // next slot to fill; oldest slot that may still be in flight
+      int issued = 0, waited = 0;
       bool stop = false;
       for (int l = 0; l < P.layers && !stop; ++l) {
         const DecLayer &Ly = P.layer[l];
         for (int s = 0; s < 4 && !stop; ++s) {
           const DecStage &S = P.st[s];
-          int64_t r0;
-          int rows_cta;
-          rows_of(S, r0, rows_cta);
+          const StageRows G = geo[s];
           for (int m = 0; m < S.count && !stop; ++m) {
-            const uint8_t *wm = Ly.w[kStageMat[s][m]];
-            const uint8_t *sm = Ly.s[kStageMat[s][m]];
-            for (int lo = 0; lo < rows_cta; lo += S.rps, ++gs) {
-              const int b = gs % P.nslots;
-              if (gs >= P.nslots && !mbar_wait(&empty[b], (uint32_t)((gs / P.nslots) - 1) & 1u)) {
+            const uint8_t *wm = Ly.w[kStageMat[s][m]] + (int64_t)G.r0 * S.row_bytes;
+            const uint8_t *sm = Ly.s[kStageMat[s][m]] + (int64_t)G.r0 * S.srow_bytes;
+            for (int lo = 0; lo < G.n; lo += S.rps, ++issued, rp.next(P.nslots)) {
+              if (issued >= P.nslots && !mbar_wait(&empty[rp.b], rp.phase ^ 1u)) {
                 set_status(P.status, kStatusTimeout);
                 stop = true;
                 break;
               }
               // at most `inflight` slots issued and not yet landed: a shorter
               // memory queue keeps the barrier's and the input loads' latency low
-              if (P.inflight > 0 && gs >= P.inflight) {
-                const int g2 = gs - P.inflight;
-                if (!mbar_wait(&full[g2 % P.nslots], (uint32_t)(g2 / P.nslots) & 1u)) {
+              for (; P.inflight > 0 && issued - waited >= P.inflight; ++waited, landed.next(P.nslots)) {
+                if (!mbar_wait(&full[landed.b], landed.phase)) {
                   set_status(P.status, kStatusTimeout);
                   stop = true;
                   break;
                 }
               }
-              const int n = min(S.rps, rows_cta - lo);
+              if (stop) break;
+              const int n = min(S.rps, G.n - lo);
               const uint32_t wbytes = (uint32_t)n * (uint32_t)S.row_bytes;
               const uint32_t sbytes = (uint32_t)n * (uint32_t)S.srow_bytes;
-              uint8_t *dst = ring + (size_t)b * P.slot_bytes;
-              mbar_arrive_expect_tx(&full[b], wbytes + sbytes);
-              bulk_g2s_hint(dst, wm + (r0 + lo) * S.row_bytes, wbytes, &full[b], pol);
-              bulk_g2s(dst + (size_t)S.rps * S.row_bytes, sm + (r0 + lo) * S.srow_bytes, sbytes, &full[b]);
+              uint8_t *dst = ring + (size_t)rp.b * P.slot_bytes;
+              mbar_arrive_expect_tx(&full[rp.b], wbytes + sbytes);
+              bulk_g2s_hint(dst, wm + (int64_t)lo * S.row_bytes, wbytes, &full[rp.b], pol);
+              bulk_g2s(dst + (size_t)S.rps * S.row_bytes, sm + (int64_t)lo * S.srow_bytes, sbytes, &full[rp.b]);
             }
           }
         }
       }
-      // every copy issued must land before the CTA may exit
-      for (int g2 = max(0, gs - P.nslots); g2 < gs; ++g2)
-        if (!mbar_wait(&full[g2 % P.nslots], (uint32_t)(g2 / P.nslots) & 1u)) set_status(P.status, kStatusTimeout);
+      // every copy issued must land before the CTA may exit: the last
+      // min(issued, nslots) slots (the earlier ones were consumed)
+      for (; waited < issued - P.nslots; ++waited) landed.next(P.nslots);
+      for (; waited < issued; ++waited, landed.next(P.nslots))
+        if (!mbar_wait(&full[landed.b], landed.phase)) set_status(P.status, kStatusTimeout);
     }
     return;
   }
@@ -418,11 +439,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   constexpr int JH = NH / 4, JI = NI / 4;  // 8-element groups per thread (NT = 512)
   const int ctid = threadIdx.x;
   const int64_t h = P.st[1].rows, inter = P.st[2].rows;
-  int gs = 0, pair_base = 0, bk = 0;
+  RingPos rp;
+  int pair_base = 0, bk = 0;
   uint32_t mx = 0;
   bool stop = false;
-  int64_t r0;
-  int nr;
   if (ctid == 0) *bar_base = barrier_base(P.bar_count);
   // RMSNorm weights of this thread's groups for the next RMSNorm (stage 1
   // or 3): each vector is loaded before the grid barrier that precedes its
@@ -445,10 +465,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
     {
       float v[JH][8];
       load_groups<JH>(h_in(), (int)(h / 8), ctid, v);
-      prep_groups<JH>((int)h, kPrepRms, v, nw, P.eps, 0.0f, xb, P.q[0], P.scales + 0, red, ctid);
-      rows_of(P.st[0], r0, nr);
-      consume_matrix<NH>(P, P.st[0], PlainOut{P.qkv}, xb, ring, full, empty, r0, nr, gs, pair_base, mx, stop, warp,
-                         lane);
+      prep_groups<JH, kPrepRms>((int)h, v, nw, P.eps, 0.0f, xb, P.q[0], P.scales + 0, red, ctid);
+      consume_matrix<NH>(P.st[0], geo[0], PlainOut{P.qkv}, xb, P.gshift, ring, P.slot_bytes, P.nslots, full, empty,
+                         rp, pair_base, mx, stop, warp, lane, P.status);
     }
     grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
 
@@ -456,10 +475,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
     {
       float v[JH][8];
       load_groups<JH>(P.qkv + 2 * h, (int)(h / 8), ctid, v);
-      prep_groups<JH>((int)h, kPrepPlain, v, nw, P.eps, 0.0f, xb, P.q[1], P.scales + 1, red, ctid);
-      rows_of(P.st[1], r0, nr);
-      consume_matrix<NH>(P, P.st[1], ResidualOut{P.h2, h_in()}, xb, ring, full, empty, r0, nr, gs, pair_base, mx,
-                         stop, warp, lane);
+      prep_groups<JH, kPrepPlain>((int)h, v, nw, P.eps, 0.0f, xb, P.q[1], P.scales + 1, red, ctid);
+      consume_matrix<NH>(P.st[1], geo[1], ResidualOut{P.h2, h_in()}, xb, P.gshift, ring, P.slot_bytes, P.nslots,
+                         full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
     }
     load_groups<JH>(P.layer[l].norm2_w, (int)(h / 8), ctid, nw);
     grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
@@ -468,13 +486,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
     {
       float v[JH][8];
       load_groups<JH>(P.h2, (int)(h / 8), ctid, v);
-      prep_groups<JH>((int)h, kPrepRms, v, nw, P.eps, 0.0f, xb, P.q[2], P.scales + 2, red, ctid);
-      rows_of(P.st[2], r0, nr);
-      consume_matrix<NH>(P, P.st[2], PlainOut{P.gate}, xb, ring, full, empty, r0, nr, gs, pair_base, mx, stop,
-                         warp, lane);
+      prep_groups<JH, kPrepRms>((int)h, v, nw, P.eps, 0.0f, xb, P.q[2], P.scales + 2, red, ctid);
+      consume_matrix<NH>(P.st[2], geo[2], PlainOut{P.gate}, xb, P.gshift, ring, P.slot_bytes, P.nslots, full, empty,
+                         rp, pair_base, mx, stop, warp, lane, P.status);
       consumers_sync<kDecCW>();  // gate rows (any warp) before the up pass reads them
-      consume_matrix<NH>(P, P.st[2], SiluMulOut{P.up, P.gate, P.act, amax_cta}, xb, ring, full, empty, r0, nr, gs,
-                         pair_base, mx, stop, warp, lane);
+      consume_matrix<NH>(P.st[2], geo[2], SiluMulOut{P.up, P.gate, P.act, amax_cta}, xb, P.gshift, ring,
+                         P.slot_bytes, P.nslots, full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
       consumers_sync<kDecCW>();
       if (ctid == 0) {
         atomicMax(P.amax, *amax_cta);
@@ -488,11 +505,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
       float v[JI][8];
       const float amax = __uint_as_float(__ldcg(P.amax));
       load_groups<JI>(P.act, (int)(inter / 8), ctid, v);
-      float unused[JI][8] = {};
-      prep_groups<JI>((int)inter, kPrepAmaxGiven, v, unused, P.eps, amax, xb, P.q[3], P.scales + 3, red, ctid);
-      rows_of(P.st[3], r0, nr);
-      consume_matrix<NI>(P, P.st[3], ResidualOut{h_out(), P.h2}, xb, ring, full, empty, r0, nr, gs, pair_base, mx,
-                         stop, warp, lane);
+      prep_groups<JI, kPrepAmaxGiven>((int)inter, v, nw, P.eps, amax, xb, P.q[3], P.scales + 3, red, ctid);
+      consume_matrix<NI>(P.st[3], geo[3], ResidualOut{h_out(), P.h2}, xb, P.gshift, ring, P.slot_bytes, P.nslots,
+                         full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
     }
     if (l + 1 < P.layers) {
       load_groups<JH>(P.layer[l + 1].norm1_w, (int)(h / 8), ctid, nw);
