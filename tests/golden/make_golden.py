@@ -1,9 +1,9 @@
 """Generate the committed golden fixtures for the quantized GEMV parity tests.
 
-Run in a checkout that has the reference tree (default /root/reference) and
-its C library built by `make -C oracle ref`:
+Run with the reference tree named (--ref, or the KS_REFERENCE_DIR
+environment variable) and its C library built by `make -C oracle ref`:
 
-    python tests/golden/make_golden.py [--ref /path/to/reference]
+    python tests/golden/make_golden.py --ref /path/to/reference
 
 Writes two files next to this script:
 
@@ -26,6 +26,7 @@ GPU hosts never read the reference tree: tests use only these files.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import sys
@@ -126,8 +127,11 @@ def seeded_cases() -> tuple[dict, dict]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("KS_REFERENCE_DIR"),
+                    help="the reference tree (default: $KS_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("name the reference tree with --ref or KS_REFERENCE_DIR")
     ref = Path(args.ref)
     smoke = smoke_bundles(ref)
     (HERE / "reference_smoke.json").write_text(json.dumps(smoke, indent=1, sort_keys=True) + "\n")
