@@ -90,16 +90,22 @@ int ks_b200_matvec_w4a8_f16(const int8_t *input, const uint8_t *packed_weights,
  * Its scratch is a fixed 540,928-byte array in device memory that every GPU
  * which loads the library holds until the process exits.
  *
- * Same arguments, checks, results and return codes as
- * ks_b200_matvec_w4a8_f16, with these limits:
- *   - rows <= 131072 and cols <= 16384, else KS_ERR_INVALID_ARG;
+ * Same arguments, checks and results as ks_b200_matvec_w4a8_f16 (it runs the
+ * same kernels: outputs are bitwise equal; on a bad scale the rows from the
+ * first bad one keep their contents), with these limits:
+ *   - rows <= 131072 and cols <= 16384, else KS_ERR_UNSUPPORTED (valid
+ *     arguments this entry point cannot serve; invalid ones still return
+ *     KS_ERR_INVALID_ARG);
  *   - packed_weights and weight_scales_f16 must be device memory (they are
- *     not staged), else KS_ERR_INVALID_ARG; input and output may be host
- *     or device memory;
+ *     not staged), else KS_ERR_UNSUPPORTED; input and output may be host
+ *     memory (staged through the array) or device memory on the weights'
+ *     GPU (used in place; another GPU is KS_ERR_INVALID_ARG);
  *   - the first call on a device looks up the scratch array's device address
- *     for that device, so make it before any stream capture;
+ *     for that device, so make it before any stream capture; the address is
+ *     cached, so no call may follow a cudaDeviceReset;
  *   - every call uses the same scratch array: calls whose work overlaps on
  *     the GPU (from several host threads) race and must be serialised.
+ * The caller's current device is the same after the call as before it.
  */
 int ks_b200_matvec_w4a8_f16_noalloc(const int8_t *input,
                                     const uint8_t *packed_weights,

@@ -96,9 +96,14 @@ Where classify(const void *p) {
   return w;
 }
 
-// A synchronous call's buffers, resolved to device addresses.
+// A synchronous call's buffers, resolved to device addresses.  The caller's
+// current device is put back when the call returns.
 class SyncCall {
  public:
+  ~SyncCall() {
+    if (prev_dev_ >= 0 && prev_dev_ != dev_) cudaSetDevice(prev_dev_);
+  }
+
   // Pick the device from the device-resident buffers (all must agree) or the
   // thread's current device, and make it current.
   int begin(const void *const *ptrs, int n) {
@@ -107,6 +112,10 @@ class SyncCall {
     if (e != cudaSuccess || devcount == 0) {
       cudaGetLastError();
       return fail(KS_ERR_DEVICE, "no CUDA device available for the B200 kernels");
+    }
+    if (cudaGetDevice(&prev_dev_) != cudaSuccess) {
+      cudaGetLastError();
+      prev_dev_ = -1;
     }
     dev_ = -1;
     for (int i = 0; i < n; ++i) {
@@ -203,6 +212,7 @@ class SyncCall {
  private:
   Where where_[8];
   int dev_ = -1;
+  int prev_dev_ = -1;
   uint32_t *status_dev_ = nullptr;
   void *copy_back_host_ = nullptr;
   void *copy_back_dev_ = nullptr;
