@@ -79,13 +79,6 @@ struct W4GemmParams {
   int32_t nbuf;       // TMEM accumulator buffers (stages the MMA may run ahead of the epilogue)
   uint32_t tmem_cols;
   uint32_t *status;
-  // the CTA's weight and scale rows, for the L2 prefetch at the start
-  const uint8_t *w;
-  int64_t wstride;     // bytes between packed rows
-  const uint8_t *s;
-  int64_t sstride_b;   // bytes between scale rows
-  int32_t w_row_bytes, s_row_bytes;
-  int32_t l2_prefetch;
 };
 
 // 8 signed int4 (value 2b in the low nibble of byte b, 2b + 1 in the high
@@ -162,28 +155,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_a);
       prefetch_tmap(&tmap_s);
-      // The whole slab of this CTA's packed weight rows and scale rows goes to
-      // L2 first (read-only data: no need to wait for the previous kernel), so
-      // HBM streams at full rate while the stage ring, only two stages deep,
-      // loads from L2 at L2 latency.
-      if (p.l2_prefetch) {
-        // (bulk prefetches take 16-byte multiples: packed rows always are,
-        // since k is a multiple of 32; scale rows are checked)
-        const int nrows = min(p.tile_rows, p.n - row0);
-        if (p.wstride == p.w_row_bytes && (int64_t)nrows * p.w_row_bytes < (int64_t(1) << 31)) {
-          bulk_prefetch_l2(p.w + (int64_t)row0 * p.wstride, (uint32_t)(nrows * p.w_row_bytes));
-        } else {
-          for (int r = 0; r < nrows; ++r) bulk_prefetch_l2(p.w + (int64_t)(row0 + r) * p.wstride, (uint32_t)p.w_row_bytes);
-        }
-        if (p.s_row_bytes % 16 == 0) {
-          if (p.sstride_b == p.s_row_bytes) {
-            bulk_prefetch_l2(p.s + (int64_t)row0 * p.sstride_b, (uint32_t)(nrows * p.s_row_bytes));
-          } else {
-            for (int r = 0; r < nrows; ++r)
-              bulk_prefetch_l2(p.s + (int64_t)(row0 + r) * p.sstride_b, (uint32_t)p.s_row_bytes);
-          }
-        }
-      }
       pdl_wait();
       const uint64_t pol = l2_policy_evict_first();
       const uint32_t tx_block = (uint32_t)(p.tile_rows * kPacked + MPAD * kStageK);
@@ -425,14 +396,6 @@ cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int d
   p.n = (int32_t)a.n;
   p.k = (int32_t)a.k;
   p.status = a.status;
-  p.w = a.w;
-  p.wstride = a.wstride;
-  p.s = static_cast<const uint8_t *>(a.s);
-  p.sbytes = a.stype == kScaleF16 ? 2 : 4;
-  p.sstride_b = a.sstride * p.sbytes;
-  p.w_row_bytes = (int32_t)(a.k / 2);
-  p.s_row_bytes = (int32_t)(a.k / a.group * p.sbytes);
-  p.l2_prefetch = env_int("KS_B200_W4GEMM_L2", 1);
   const int mpad = (int)((a.m + 15) / 16 * 16);
   p.nkb = (int32_t)((a.k + kStageK - 1) / kStageK);
   p.gps = (int32_t)(kStageK / a.group) > 0 ? (int32_t)(kStageK / a.group) : 1;
