@@ -486,6 +486,44 @@ int ks_b200_quantize_per_token_async(const float *x, size_t ldx, size_t n_tokens
 int ks_b200_quant_layout_version(void);
 
 /*
+ * Resident W4A8 weights (no counterpart in the reference, whose calls read
+ * the weights from the caller's memory every time): upload rows
+ * [row_begin, row_begin + row_count) of a packed matrix -- all of it, or one
+ * rank's row shard -- to the current device once and run GEMVs on them.
+ * The rows are copied byte for byte in the ABI layout; only the row strides
+ * grow to multiples of 16 bytes (zero padding, never read).  The source may
+ * be host or device memory.  layout_version must be KS_QUANT_LAYOUT_VERSION
+ * (the layout the caller's converter wrote; DES-015:195-198 proposes the
+ * macro), else KS_ERR_UNSUPPORTED; other argument checks as for
+ * ks_matvec_w4a8, plus row_begin + row_count <= rows, else
+ * KS_ERR_INVALID_ARG.  Allocates device memory, freed by
+ * ks_b200_w4a8_release.
+ */
+typedef struct ks_b200_w4a8_weights ks_b200_w4a8_weights;
+int ks_b200_w4a8_register(const uint8_t *packed_weights,
+                          size_t packed_stride_bytes, const void *weight_scales,
+                          int scale_type, size_t scale_stride, size_t rows,
+                          size_t cols, size_t group_size, size_t row_begin,
+                          size_t row_count, int layout_version,
+                          ks_b200_w4a8_weights **out);
+/* The device copy: pointers, strides (bytes / elements), rows held and the
+ * first source row (any output pointer may be NULL). */
+int ks_b200_w4a8_weights_info(const ks_b200_w4a8_weights *weights,
+                              const uint8_t **packed_weights,
+                              size_t *packed_stride_bytes,
+                              const void **weight_scales, size_t *scale_stride,
+                              size_t *rows, size_t *row_begin);
+/* ks_b200_matvec_w4a8_async over the registered rows (output[r] for row
+ * row_begin + r), with the registration's device current. */
+int ks_b200_w4a8_matvec_registered_async(const ks_b200_w4a8_weights *weights,
+                                         const int8_t *input, float input_scale,
+                                         int32_t input_zero_point,
+                                         int32_t weight_zero_point,
+                                         float *output, uint32_t *status,
+                                         void *stream);
+int ks_b200_w4a8_release(ks_b200_w4a8_weights *weights);
+
+/*
  * GGML Q4_0 weights -> native W4A8, on the GPU (the reference's offline
  * conversion, DES-015:148-179; no counterpart function in the reference).
  * blocks: rows x (cols/32) Q4_0 blocks of 18 bytes (f16 d, then 16 bytes:

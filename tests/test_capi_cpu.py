@@ -179,6 +179,7 @@ def test_wait_and_status_check_argument_checks(ks):
     """The bounded peer wait and the status check reject bad arguments on the
     host, before any CUDA call."""
     L = ks.lib()
+    assert ks.KS_QUANT_LAYOUT_VERSION == L.ks_b200_quant_layout_version()
     buf = np.zeros(64, np.uint32)
     a = ks.addr(buf)
     assert L.ks_b200_peer_arrival_wait_ranks_async(None, 2, a, 1, 0, None, None) == ks.KS_ERR_INVALID_ARG
@@ -213,3 +214,23 @@ def test_decode_layers_argument_checks(ks):
                                               None, None) == ks.KS_ERR_INVALID_ARG
     assert L.ks_b200_decode_layers_w4a8_async(2, a, a, norms, norms, 0.0, ptrs, ptrs, h, i, 32, a, one + 32768,
                                               None, None) == ks.KS_ERR_INVALID_ARG
+
+
+def test_resident_weights_argument_checks(ks):
+    """Registration refuses a layout version other than the library's, and
+    bad shapes, before touching a GPU."""
+    import ctypes
+
+    L = ks.lib()
+    w = np.zeros((4, 16), np.uint8)
+    s = np.zeros((4, 1), np.float32)
+    h = ctypes.c_void_p()
+    args = (ks.addr(w), 16, ks.addr(s), ks.SCALE_F32, 1, 4, 32, 32)
+    assert L.ks_b200_w4a8_register(*args, 0, 4, 2, ctypes.byref(h)) == ks.KS_ERR_UNSUPPORTED
+    assert "version 2" in ks.last_error() and h.value is None
+    assert L.ks_b200_w4a8_register(*args, 3, 2, 1, ctypes.byref(h)) == ks.KS_ERR_INVALID_ARG  # rows 3..4 beyond 4
+    assert L.ks_b200_w4a8_register(*args, 0, 0, 1, ctypes.byref(h)) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_w4a8_register(ks.addr(w), 8, ks.addr(s), ks.SCALE_F32, 1, 4, 32, 32, 0, 4, 1,
+                                   ctypes.byref(h)) == ks.KS_ERR_INVALID_ARG  # stride < 16 bytes
+    assert L.ks_b200_w4a8_register(*args, 0, 4, 1, None) == ks.KS_ERR_INVALID_ARG
+    assert L.ks_b200_w4a8_release(None) == ks.KS_OK

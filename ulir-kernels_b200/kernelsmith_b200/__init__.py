@@ -36,6 +36,7 @@ STATUS_WORDS = 2
 STATUS_BAD_SCALE = 0
 STATUS_TIMEOUT = 1
 IPC_HANDLE_BYTES = 64
+KS_QUANT_LAYOUT_VERSION = 1  # include/ks_b200.h; lib().ks_b200_quant_layout_version() returns the built value
 
 _vp = c_void_p
 _sz = c_size_t
@@ -122,6 +123,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, _vp, _sz, _vp, _vp, _sz, _vp, _f, _vp, _sz, _sz, _sz, _sz, _vp, _vp],
     ),
     "ks_b200_quant_layout_version": (c_int, []),
+    "ks_b200_w4a8_register": (c_int, [_vp, _sz, _vp, c_int, _sz, _sz, _sz, _sz, _sz, _sz, c_int, _vp]),
+    "ks_b200_w4a8_weights_info": (c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "ks_b200_w4a8_matvec_registered_async": (c_int, [_vp, _vp, _f, _i32, _i32, _vp, _vp, _vp]),
+    "ks_b200_w4a8_release": (c_int, [_vp]),
     "ks_b200_gemm_w4a8_async": (
         c_int,
         [_vp, _sz, _vp, _vp, _sz, _vp, c_int, _sz, _vp, _sz, _sz, _sz, _sz, _sz, _vp, _vp],
