@@ -240,8 +240,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < nb; ++j) {
           const uint8_t *src = st + pk_off + j * p.pk_bytes + (size_t)r * kPacked;
           uint8_t *dst = st + j * kOpBytes + (size_t)r * kStageK;
+          // 16 packed bytes = 32 weights = two 16-byte output chunks.  The
+          // chunk order rotates with lane / 8: packed rows are 64 bytes apart,
+          // so the 32 lanes reading chunk q together would hit 8 of the 32
+          // banks (16-way conflicts); rotated they cover all banks, and each
+          // group of 8 rows keeps one chunk, so the swizzled 16-byte stores
+          // below stay conflict-free too.
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {  // 16 packed bytes = 32 weights = two 16-byte output chunks
+          for (int q0 = 0; q0 < 4; ++q0) {
+            const int q = (q0 + (lane >> 3)) & 3;
             const uint4 v = lds128(src + 16 * q);
             uint32_t o[8];
             unpack8x16(v.x, o[0], o[1]);
@@ -303,16 +310,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_ld(v0, v1);
         tc_wait_ld(v2, v3);  // nothing left to wait for: passes v2, v3 through the wait
         float sc[GPC];
+        // the box holds tile_rows rows: lanes at and above them have no weight row
+        const int gi0 = gbase + g0;  // first scale index of the batch inside the box row
+        if (r < p.tile_rows && g0 + GPC <= ng && gi0 % GPC == 0 && (gi0 + GPC) * p.sbytes <= p.sbox) {
+          // the batch's scales in one vector load (rows are sbox bytes apart:
+          // one load per batch instead of GPC conflicting 2- or 4-byte loads)
+          if (p.sbytes == 2) {
+            uint32_t h[(GPC + 1) / 2];
+            if constexpr (GPC == 4) {
+              const uint2 t = *reinterpret_cast<const uint2 *>(srow + 2 * gi0);
+              h[0] = t.x;
+              h[1] = t.y;
+            } else if constexpr (GPC == 2) {
+              h[0] = *reinterpret_cast<const uint32_t *>(srow + 2 * gi0);
+            } else {
+              h[0] = *reinterpret_cast<const uint16_t *>(srow + 2 * gi0);
+            }
 #pragma unroll
-        for (int gg = 0; gg < GPC; ++gg) {
-          // the box holds tile_rows rows: lanes at and above them have no weight row
-          const int gi = gbase + g0 + gg;  // scale index inside the box row
-          sc[gg] = 0.0f;
-          if (r < p.tile_rows && g0 + gg < ng)
-            sc[gg] = p.sbytes == 2 ? __half2float(*reinterpret_cast<const __half *>(srow + 2 * gi))
-                                   : *reinterpret_cast<const float *>(srow + 4 * gi);
-          sc[gg] = __fmul_rn(sc[gg], 0.0625f);  // the operand holds 16 x the weights
+            for (int gg = 0; gg < GPC; ++gg)
+              sc[gg] = __half2float(__ushort_as_half((unsigned short)(h[gg / 2] >> (16 * (gg & 1)))));
+          } else {
+            if constexpr (GPC == 4) {
+              const float4 t = *reinterpret_cast<const float4 *>(srow + 4 * gi0);
+              sc[0] = t.x;
+              sc[1] = t.y;
+              sc[2] = t.z;
+              sc[3] = t.w;
+            } else if constexpr (GPC == 2) {
+              const float2 t = *reinterpret_cast<const float2 *>(srow + 4 * gi0);
+              sc[0] = t.x;
+              sc[1] = t.y;
+            } else {
+              sc[0] = *reinterpret_cast<const float *>(srow + 4 * gi0);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int gg = 0; gg < GPC; ++gg) {
+            const int gi = gi0 + gg;
+            sc[gg] = 0.0f;
+            if (r < p.tile_rows && g0 + gg < ng)
+              sc[gg] = p.sbytes == 2 ? __half2float(*reinterpret_cast<const __half *>(srow + 2 * gi))
+                                     : *reinterpret_cast<const float *>(srow + 4 * gi);
+          }
         }
+#pragma unroll
+        for (int gg = 0; gg < GPC; ++gg) sc[gg] = __fmul_rn(sc[gg], 0.0625f);  // the operand holds 16 x the weights
 #pragma unroll
         for (int f = 0; f < GPC * MPAD && f < 64; ++f) {
           const uint32_t u = f < 16 ? v0[f & 15] : f < 32 ? v1[f & 15] : f < 48 ? v2[f & 15] : v3[f & 15];
