@@ -1077,7 +1077,7 @@ def run_gemm_w4a8(K, torch, dev):
     stream = torch.cuda.Stream(device=dev)
     peak, _ = measured_hbm_peak()
     out = {"shape": "M x 4096 x 14336 int8 x W4A8 (G 32, f16 scales) -> f32",
-           "kernel": "gemm_w4a8_tc_kernel (int4 unpacked to int8 in shared memory, tcgen05.mma kind::i8)"}
+           "kernel": "gemm_w4a8_tc_kernel (int4 widened to int8 into tensor memory, tcgen05.mma kind::i8 with the A operand in TMEM)"}
     for M in (8, 16, 32, 64):
         A = torch.randint(-127, 128, (M, Kd), dtype=torch.int8, device=dev, generator=gen)
         sx = torch.rand(M, device=dev, generator=gen) * 0.02 + 0.01

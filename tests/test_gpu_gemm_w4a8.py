@@ -72,7 +72,10 @@ def test_bench_shape_sampled_rows(ks, cuda, oracle, m):
 
 @pytest.mark.parametrize("shape", [(1, 256, 128, 128, True), (16, 1000, 4096, 64, False), (33, 500, 11008, 32, True),
                                    (64, 384, 2048, 32, False), (5, 130, 512, 128, False), (48, 208, 4096, 64, True),
-                                   (8, 300, 384, 32, True), (8, 300, 640, 64, True), (12, 96, 1152, 128, False)])
+                                   (8, 300, 384, 32, True), (8, 300, 640, 64, True), (12, 96, 1152, 128, False),
+                                   (32, 300, 2048, 32, True), (24, 200, 1024, 128, False), (64, 256, 4096, 64, True),
+                                   (40, 150, 512, 128, True), (64, 200, 640, 128, False), (20, 100, 384, 64, True),
+                                   (17, 64, 33 * 128, 32, False), (2, 4000, 2048, 32, True)])
 def test_shapes_all_rows(ks, cuda, oracle, shape):
     import torch
 
@@ -103,3 +106,32 @@ def test_unsupported_shapes(ks, cuda):
     assert L.ks_b200_gemm_w4a8_async(p, 128, p, p, 64, p, 1, 8, p, 64, 65, 64, 128, 32, None, None) == U  # m > 64
     assert L.ks_b200_gemm_w4a8_async(p, 128, p, p, 64, p, 1, 8, p, 64, 8, 64, 128, 256, None, None) == U  # group
     assert L.ks_b200_gemm_w4a8_async(p, 130, p, p, 64, p, 1, 8, p, 64, 8, 64, 128, 32, None, None) == U  # lda % 16
+
+
+@pytest.mark.parametrize("m", [1, 8, 16, 33, 64])
+def test_no_bounded_wait_runs_out(ks, cuda, m):
+    """Every wait in the kernel is bounded at about a second and records a
+    timeout in the status word; a wait that ran out unreported would still
+    give correct results, one second late.  20 launches of the bench shape
+    must take far less than one second in all."""
+    import torch
+
+    n, k, group = 14336, 4096, 32
+    g = torch.Generator(device=cuda)
+    g.manual_seed(m)
+    a = torch.randint(-127, 128, (m, k), dtype=torch.int8, device=cuda, generator=g)
+    sx = torch.rand(m, device=cuda, generator=g) * 0.02 + 0.01
+    w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=cuda, generator=g)
+    s = (torch.rand((n, k // group), device=cuda, generator=g) * 9e-3 + 1e-3).half()
+    y = torch.zeros((m, n), dtype=torch.float32, device=cuda)
+    status = torch.zeros(2, dtype=torch.int32, device=cuda)
+    ks.gemm_w4a8_async(a, sx, w, s, y, m, n, k, group, status=status)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        ks.gemm_w4a8_async(a, sx, w, s, y, m, n, k, group, status=status)
+    e1.record()
+    e1.synchronize()
+    assert status.cpu().tolist() == [0, 0]
+    assert e0.elapsed_time(e1) < 100.0, f"20 launches took {e0.elapsed_time(e1):.1f} ms"

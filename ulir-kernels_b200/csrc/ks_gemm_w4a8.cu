@@ -1,5 +1,5 @@
 // ks_gemm_w4a8.cu -- batched W4A8 GEMM for decode (M = 1..64 tokens) on 5th-
-// generation tensor cores (tcgen05.mma kind::i8, TMEM accumulators), sm_100a.
+// generation tensor cores (tcgen05.mma kind::i8, TMEM operands), sm_100a.
 //
 //   y[m, n]      = sx[m] * sum_g f32(acc_g[m, n]) * s[n, g]      (groups in order)
 //   acc_g[m, n]  = sum_{k in group g} x[m, k] * w[n, k]           (int32, exact)
@@ -11,27 +11,32 @@
 // order of the f32 sum (the reference sums per element; here per group,
 // like the GEMV kernels).
 //
-// Swap-AB as in the INT8 GEMM: weight rows fill the MMA's M = 128 (TMEM
-// lanes), tokens its N (padded to 16).  A CTA owns `tile_rows` weight rows
-// (the same share for every SM, a multiple of 16).  K streams in stages of up
-// to four 128-K blocks (one barrier round trip per stage in every hand-off;
-// each round trip costs the MMA thread a few hundred cycles).  Per block:
-//   warp 0    TMA: the packed weight tile [tile_rows x 64 B] (no swizzle),
-//             the token tile [Mpad x 128 B] (128-byte swizzle) and, once per
-//             one or more stages, a scale box [tile_rows x 16..64 B] into a
-//             small ring of its own.  No multicast.
-//   warps 2-5 unpack: one weight row each, int4 -> int8 holding 16 x the
-//             weight (shift + mask per 4 bytes, PRMT to interleave), written
-//             in the UMMA K-major 128-byte-swizzle layout; proxy fence; arrive.
-//   warp 1    MMA: per group, tcgen05.mma (K = 32 each, G / 32 of them) into
-//             the group's own TMEM column block (fresh accumulate), buffered
-//             over as many stages as 512 TMEM columns hold (at least 2, up
-//             to 8); one commit per stage frees it, one hands the buffer to
-//             the epilogue.
-//   warps 6-9 epilogue: tcgen05.ld each group's int32 accumulators (one TMEM
-//             lane per weight row), acc[m] += f32(v) * (s[n, g] / 16) in
-//             registers,
-//             release the TMEM buffer; at the end y = acc * sx.
+// Swap-AB: weight rows fill the MMA's M = 128 (TMEM lanes), tokens its N
+// (padded to 16).  A CTA owns `tile_rows` weight rows (the same share for
+// every SM, a multiple of 16).  K runs in 128-element blocks (four MMAs of
+// K = 32), four blocks per ring stage.  The int4 weights are widened to int8
+// by the CUDA cores and written straight into tensor memory, which the MMA
+// reads as its A operand, so shared memory holds only what TMA brings in
+// (packed weights and tokens, ~37 KB per stage at M <= 16: five stages in
+// flight).  Roles:
+//   warp 0      TMA: per stage two packed-weight boxes [tile_rows x 128 B]
+//               (128-byte swizzle: the unpack reads are conflict-free), four
+//               token tiles [Mpad x 128 B] (128-byte swizzle, the MMA's B
+//               operand) and, once per one or more stages, a scale box
+//               [tile_rows x 16..64 B] into a ring of its own.  No multicast.
+//   warps 2-9   unpack, two sets of four (one warp per TMEM lane quarter;
+//               even and odd blocks): one weight row per lane, int4 -> int8
+//               holding 16 x the weight (shift + mask per 4 bytes, PRMT to
+//               interleave), tcgen05.st of the row's 32 columns into one of
+//               four A slots, tcgen05.wait::st, arrive.
+//   warp 1      MMA: per block four tcgen05.mma (A from the slot, B the token
+//               tile) into the groups' accumulator columns (fresh
+//               accumulators per group), all loops unrolled with
+//               compile-time accumulate flags; commits free the A slot, the
+//               stage (its tokens) and hand the accumulators on.
+//   warps 10-13 epilogue: tcgen05.ld a unit's group accumulators (one TMEM
+//               lane per weight row), acc[m] += f32(v) * (s[n, g] / 16),
+//               release the columns; at the end y = acc * sx.
 // Every wait is bounded (about one second); a timeout is recorded in the
 // status word, the waiting role stops, and the kernel runs to its end.
 
@@ -51,103 +56,239 @@ namespace ksb {
 
 namespace {
 
-constexpr int kRows = 128;         // MMA M
-constexpr int kStageK = 128;       // K elements per stage: one 128-byte int8 swizzle row
-constexpr int kPacked = kStageK / 2;  // packed weight bytes per row per stage
-constexpr int kThreads = 320;      // 0 producer, 1 MMA, 2-5 unpack, 6-9 epilogue
+constexpr int kRows = 128;                     // MMA M = TMEM lanes
+constexpr int kBlockK = 128;                   // K per block: 32 TMEM columns of int8, four MMAs
+constexpr int kBlockPacked = kBlockK / 2;      // packed bytes per row per block
+constexpr int kSB = 4;                         // blocks per ring stage (two 128-byte packed boxes)
+constexpr int kUnpackWarps = 8;                // two sets of four: even and odd blocks
+constexpr int kEpiWarp0 = 2 + kUnpackWarps;    // first epilogue warp
+#ifndef KS_W4_NA
+#define KS_W4_NA 8
+#endif
+constexpr int kNA = KS_W4_NA;                  // A blocks in TMEM (32 columns each), where the accumulators allow
+constexpr int kTmemCols = 512;
+constexpr int kMaxStages = 8;
+constexpr int kMaxAcc = 8;
+constexpr int kMD = 16;  // "MMAs of hand-off h done" barriers: h % kMD (more than the MMA can run ahead of any waiter)
 constexpr int kScaleRing = 4;
-constexpr int kMaxStagesW4 = 8;
-constexpr int kMaxBufs = 8;
-constexpr int kOpBytes = kRows * kStageK;  // int8 weight operand of a stage
 
 struct W4GemmParams {
   float *y;
   int64_t ldy;
   const float *sx;
   int32_t m, n, k;
-  int32_t nkb;        // 128-K blocks (K / 128, rounded up)
-  int32_t bps;        // blocks per ring stage (one barrier round trip per stage in every ring)
-  int32_t nks;        // stages: nkb / bps, rounded up
-  int32_t nst;        // ring stages
+  int32_t nkb;         // 128-K blocks (K / 128, rounded up)
+  int32_t nks;         // ring stages: nkb / kSB, rounded up
+  int32_t nst;         // ring depth
   int32_t tile_rows;
-  int32_t gps;        // groups per block: 128 / G (at least 1)
-  int32_t kpg;        // MMAs (K = 32) per group: G / 32
-  int32_t sbytes;     // 2 (f16) or 4 (f32)
-  int32_t sbox;       // scale bytes per row per box: max(16, bps * gps * sbytes)
-  int32_t spb;        // stages per scale box
-  int32_t stage_bytes, a_bytes, pk_bytes, sbox_bytes;  // a_bytes, pk_bytes: per block
-  int32_t nbuf;       // TMEM accumulator buffers (stages the MMA may run ahead of the epilogue)
-  uint32_t tmem_cols;
+  int32_t box_bytes;   // one packed box: tile_rows x 128 B
+  int32_t tok_off;     // token tiles of a stage, after its two packed boxes
+  int32_t stage_bytes;
+  int32_t sbytes;      // 2 (f16) or 4 (f32)
+  int32_t sbox;        // scale bytes per row per box: max(16, kSB * groups per block * sbytes)
+  int32_t spb;         // stages per scale box
+  int32_t sbox_bytes;
   uint32_t *status;
 };
 
 // 8 signed int4 (value 2b in the low nibble of byte b, 2b + 1 in the high
-// nibble) -> 8 int8 in k order, as two words, each byte holding 16 x the
-// weight (the nibble moved to the byte's high half: exact and sign-correct).
-// The int32 group sums are then 16 x the true sums (at most 128 * 128 * 128
-// in magnitude, exact in f32) and the epilogue scales by s / 16 instead of s
-// -- a power of two, so every product and sum rounds as with the true sums.
-__device__ __forceinline__ void unpack8x16(uint32_t v, uint32_t &lo, uint32_t &hi) {
-  const uint32_t te = (v << 4) & 0xF0F0F0F0u;  // values 0, 2, 4, 6
-  const uint32_t to = v & 0xF0F0F0F0u;         // values 1, 3, 5, 7
-  lo = prmt(te, to, 0x5140);
-  hi = prmt(te, to, 0x7362);
+// nibble) -> 8 int8 as two words, each byte holding 16 x the weight (the
+// nibble moved to the byte's high half: exact and sign-correct): even k
+// (0, 2, 4, 6) in the first word, odd k in the second.  The MMA only pairs
+// A[k] with B[k], so the token tiles are put in the same order (each 8-byte
+// group of k as x0 x2 x4 x6 x1 x3 x5 x7) and the weights need no byte
+// shuffle.  The int32 group sums are 16 x the true sums (at most 2^21 in
+// magnitude) and the epilogue scales by s / 16 instead of s -- a power of
+// two, so every product and sum rounds as with the true sums.
+__device__ __forceinline__ void unpack8x16(uint32_t v, uint32_t &even, uint32_t &odd) {
+  even = (v << 4) & 0xF0F0F0F0u;
+  odd = v & 0xF0F0F0F0u;
 }
 
-template <int MPAD>
-__global__ void __launch_bounds__(kThreads, 1)
+// int32 -> f32, exact for every group sum here (|v| <= 2^21).  The plain
+// conversion measured faster than two full-rate operations on the bits of
+// 1.5 * 2^23 (29.6 against 33.7 us per GEMM at M = 32).
+__device__ __forceinline__ float i2f_small(uint32_t v) { return __int2float_rn((int)v); }
+
+// Compile-time shape of one hand-off between the roles: HB blocks (two while
+// three accumulator units of two blocks fit in TMEM beside the A slots, else
+// one), UPH accumulator units of UG groups (UCOLS columns) per hand-off, NACC
+// units after the A slots, NAS A slots of HB blocks.  Fewer, larger hand-offs
+// matter: every barrier wait and commit of the MMA thread costs about a
+// hundred cycles while the unpack and epilogue warps share its scheduler.
+template <int MPAD, int KPG>
+struct Shape {
+  static constexpr int GPS = 4 / KPG;  // groups per block
+  static constexpr int HB = GPS * MPAD <= 64 ? 2 : 1;
+  static constexpr int GPH = HB * GPS;
+  static constexpr int UPH = GPH * MPAD <= 192 ? 1 : 2;
+  static constexpr int UG = GPH / UPH;
+  static constexpr int UCOLS = UG * MPAD;
+  static constexpr int NA = (kTmemCols - kNA * 32) / UCOLS >= 2 ? kNA : 4;  // A blocks
+  static constexpr int NAS = NA / HB;
+  static constexpr int ACC0 = NA * 32;  // accumulator columns start after the A slots
+  static constexpr int NACC = (kTmemCols - ACC0) / UCOLS < kMaxAcc ? (kTmemCols - ACC0) / UCOLS : kMaxAcc;
+  // MMA issuers: two (alternate hand-offs) when each can own NPI >= UPH
+  // accumulator units and the A slots split by hand-off parity; else one.
+  // Every barrier then has one waiting role that takes its phases in order
+  // (a parity wait is only sound while the barrier is at most one phase
+  // ahead of or behind the waiter).
+  static constexpr int ISS = NACC >= 2 * UPH && NAS % 2 == 0 ? 2 : 1;
+  static constexpr int NPI = NACC / ISS;
+  static_assert(NACC >= 2 && kSB % HB == 0, "two accumulator units at least; whole hand-offs per stage");
+};
+
+// Epilogue warps -- two sets of four, each set half of the tokens -- and the
+// warp of the second MMA issuer after them (on the third scheduler).
+template <int MR>
+struct Roles {
+  static constexpr int EW = 8;
+  static constexpr int MMA2 = kEpiWarp0 + EW;
+  static constexpr int THREADS = 32 * (MMA2 + 1);
+};
+
+// A ring position kept incrementally: slot and the parity of its current use.
+struct Ring {
+  int i = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++i == n) {
+      i = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
+// UG consecutive group scales of one row of a scale box, times 1/16 (the
+// operand holds 16 x the weights); one or two vector loads.
+template <int UG>
+__device__ __forceinline__ void load_scales(const uint8_t *srow, int gi0, int sbytes, bool live, float (&sc)[UG]) {
+#pragma unroll
+  for (int g = 0; g < UG; ++g) sc[g] = 0.0f;
+  if (live) {
+    if (sbytes == 2) {
+      uint32_t h[(UG + 1) / 2];
+      const uint8_t *q = srow + 2 * gi0;
+      if constexpr (UG == 8) {
+        const uint4 t = *reinterpret_cast<const uint4 *>(q);
+        h[0] = t.x;
+        h[1] = t.y;
+        h[2] = t.z;
+        h[3] = t.w;
+      } else if constexpr (UG == 4) {
+        const uint2 t = *reinterpret_cast<const uint2 *>(q);
+        h[0] = t.x;
+        h[1] = t.y;
+      } else if constexpr (UG == 2) {
+        h[0] = *reinterpret_cast<const uint32_t *>(q);
+      } else {
+        h[0] = *reinterpret_cast<const uint16_t *>(q);
+      }
+#pragma unroll
+      for (int g = 0; g < UG; ++g)
+        sc[g] = __half2float(__ushort_as_half((unsigned short)(h[g / 2] >> (16 * (g & 1)))));
+    } else {
+      const float *q = reinterpret_cast<const float *>(srow + 4 * gi0);
+      if constexpr (UG >= 4) {
+#pragma unroll
+        for (int v = 0; v < UG / 4; ++v) {
+          const float4 t = reinterpret_cast<const float4 *>(q)[v];
+          sc[4 * v] = t.x;
+          sc[4 * v + 1] = t.y;
+          sc[4 * v + 2] = t.z;
+          sc[4 * v + 3] = t.w;
+        }
+      } else if constexpr (UG == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(q);
+        sc[0] = t.x;
+        sc[1] = t.y;
+      } else {
+        sc[0] = q[0];
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < UG; ++g) sc[g] = __fmul_rn(sc[g], 0.0625f);
+}
+
+template <int MPAD, int MR, int KPG>
+__global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
     gemm_w4a8_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_s, const W4GemmParams p) {
+  using SH = Shape<MPAD, KPG>;
+  constexpr int GPS = SH::GPS, HB = SH::HB, UPH = SH::UPH, UG = SH::UG, UCOLS = SH::UCOLS, NAS = SH::NAS,
+                NACC = SH::NACC, ISS = SH::ISS, NPI = SH::NPI;
+  constexpr int TOK_BYTES = MPAD * kBlockK;  // one token tile
+  constexpr int EW = Roles<MR>::EW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // [stage 0 .. nst-1: bps int8 operands (16 KB each) | bps token tiles | bps packed tiles]
-  // [scale boxes] [barriers]
+  // [stage 0 .. nst-1: two packed boxes | kSB token tiles] [scale boxes] [barriers]
   uint8_t *stages = smem;
   uint8_t *sboxes = smem + (size_t)p.nst * p.stage_bytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(sboxes + (size_t)kScaleRing * p.sbox_bytes);
-  uint64_t *full = bars;                      // [nst]  TMA landed
-  uint64_t *unpacked = full + kMaxStagesW4;   // [nst]  int8 operands written
-  uint64_t *empty = unpacked + kMaxStagesW4;  // [nst]  MMAs of the stage done
-  uint64_t *mma_done = empty + kMaxStagesW4;  // [nbuf] TMEM buffer ready
-  uint64_t *tmem_free = mma_done + kMaxBufs;  // [nbuf] TMEM buffer read
-  uint64_t *sfull = tmem_free + kMaxBufs;     // [ring] scale box landed
-  uint64_t *sempty = sfull + kScaleRing;      // [ring] scale box used
+  uint64_t *full = bars;                        // [nst]  TMA landed
+  uint64_t *empty = full + kMaxStages;          // [nst]  unpacked by all eight warps and its MMAs done
+  uint64_t *afull = empty + kMaxStages;         // [NAS]  A slot written
+  uint64_t *mdone = afull + 8;                // [kMD]  MMAs of a hand-off done: A slot free, accumulators ready
+  uint64_t *accempty = mdone + kMD;             // [NACC] accumulator unit read
+  uint64_t *sfull = accempty + kMaxAcc;         // [ring] scale box landed
+  uint64_t *sempty = sfull + kScaleRing;        // [ring] scale box used
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sempty + kScaleRing);
   volatile uint32_t *abort_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * p.tile_rows;
-  const int tok_off = p.bps * kOpBytes;                  // token tiles of a stage
-  const int pk_off = p.bps * (kOpBytes + p.a_bytes);     // packed tiles of a stage
-  auto blocks_of = [&](int ks) { return min(p.bps, p.nkb - ks * p.bps); };
+  const int nh = (p.nkb + HB - 1) / HB;  // hand-offs
+  auto blocks_of = [&](int ks) { return min(kSB, p.nkb - ks * kSB); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.nst; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&unpacked[s], 4);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kUnpackWarps + ISS);  // eight unpack warps, one commit per MMA issuer
     }
-    for (int b = 0; b < p.nbuf; ++b) {
-      mbar_init(&mma_done[b], 1);
-      mbar_init(&tmem_free[b], 4);
-    }
+    for (int a = 0; a < NAS; ++a) mbar_init(&afull[a], 4 * HB);  // the warps of the sets writing the slot's blocks
+    for (int b = 0; b < kMD; ++b) mbar_init(&mdone[b], 1);
+    for (int b = 0; b < NACC; ++b) mbar_init(&accempty[b], EW);
     for (int b = 0; b < kScaleRing; ++b) {
       mbar_init(&sfull[b], 1);
-      mbar_init(&sempty[b], 4);
+      mbar_init(&sempty[b], EW);
     }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
+  // ---------------------------------------------------------------- producer --
+  const uint64_t pol = l2_policy_evict_first();
+  int issued = 0, boxes = 0;
+  auto issue_stage = [&](int ks) -> bool {
+    const int s = ks % p.nst;
+    if (ks >= p.nst && !mbar_wait(&empty[s], (uint32_t)((ks / p.nst) - 1) & 1u)) return false;
+    if (ks % p.spb == 0) {
+      const int bi = ks / p.spb, sb = bi % kScaleRing;
+      if (bi >= kScaleRing && !mbar_wait(&sempty[sb], (uint32_t)((bi / kScaleRing) - 1) & 1u)) return false;
+      mbar_arrive_expect_tx(&sfull[sb], (uint32_t)(p.tile_rows * p.sbox));
+      tma_load_2d(sboxes + (size_t)sb * p.sbox_bytes, &tmap_s, bi * p.sbox, row0, &sfull[sb]);
+      ++boxes;
+    }
+    const int nb = blocks_of(ks), npk = (nb + 1) / 2;
+    uint8_t *st = stages + (size_t)s * p.stage_bytes;
+    mbar_arrive_expect_tx(&full[s], (uint32_t)(npk * p.box_bytes + nb * TOK_BYTES));
+    for (int b = 0; b < npk; ++b)
+      tma_load_2d_hint(st + b * p.box_bytes, &tmap_w, (ks * kSB + 2 * b) * kBlockPacked, row0, &full[s], pol);
+    for (int j = 0; j < nb; ++j)
+      tma_load_2d(st + p.tok_off + j * TOK_BYTES, &tmap_a, (ks * kSB + j) * kBlockK, 0, &full[s]);
+    ++issued;
+    return true;
+  };
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(p.tmem_cols)
+                 "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_d = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer --
@@ -156,36 +297,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&tmap_a);
       prefetch_tmap(&tmap_s);
       pdl_wait();
-      const uint64_t pol = l2_policy_evict_first();
-      const uint32_t tx_block = (uint32_t)(p.tile_rows * kPacked + MPAD * kStageK);
-      int issued = 0, boxes = 0;
       for (int ks = 0; ks < p.nks; ++ks) {
-        const int s = ks % p.nst;
-        if (ks >= p.nst && !mbar_wait(&empty[s], (uint32_t)((ks / p.nst) - 1) & 1u)) {
+        if (!issue_stage(ks)) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
-        if (ks % p.spb == 0) {
-          const int bi = ks / p.spb, sb = bi % kScaleRing;
-          if (bi >= kScaleRing && !mbar_wait(&sempty[sb], (uint32_t)((bi / kScaleRing) - 1) & 1u)) {
-            set_status(p.status, kStatusTimeout);
-            *abort_flag = 1;
-            break;
-          }
-          mbar_arrive_expect_tx(&sfull[sb], (uint32_t)(p.tile_rows * p.sbox));
-          tma_load_2d(sboxes + (size_t)sb * p.sbox_bytes, &tmap_s, bi * p.sbox, row0, &sfull[sb]);
-          ++boxes;
-        }
-        const int nb = blocks_of(ks);
-        uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)nb * tx_block);
-        for (int j = 0; j < nb; ++j) {
-          const int kb = ks * p.bps + j;
-          tma_load_2d_hint(st + pk_off + j * p.pk_bytes, &tmap_w, kb * kPacked, row0, &full[s], pol);
-          tma_load_2d(st + tok_off + j * p.a_bytes, &tmap_a, kb * kStageK, 0, &full[s]);
-        }
-        ++issued;
       }
       pdl_trigger();
       for (int ks = max(0, issued - p.nst); ks < issued; ++ks)
@@ -194,186 +311,241 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&sfull[bi % kScaleRing], (uint32_t)(bi / kScaleRing) & 1u))
           set_status(p.status, kStatusTimeout);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == Roles<MR>::MMA2) {
     // ----------------------------------------------------------------- MMA --
-    if (lane == 0) {
+    // Two issuing threads on different schedulers take alternate hand-offs
+    // (each MMA instruction costs its thread tens of cycles of issue while
+    // the unpack and epilogue warps share the scheduler); their hand-offs use
+    // different A slots and accumulator columns, and each commits its own.
+    const int mine = warp == 1 ? 0 : 1;
+    if (lane == 0 && mine < ISS) {
       const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MPAD >> 3) << 17) |
                              ((uint32_t)(kRows >> 4) << 24);
-      for (int ks = 0; ks < p.nks; ++ks) {
-        const int s = ks % p.nst, b = ks % p.nbuf;
-        if (!mbar_wait(&unpacked[s], (uint32_t)(ks / p.nst) & 1u) ||
-            (ks >= p.nbuf && !mbar_wait(&tmem_free[b], (uint32_t)((ks / p.nbuf) - 1) & 1u))) {
+      Ring st, as, ac;  // stage, A slot, this issuer's next accumulator unit (of its own NPI)
+      int j0 = 0;       // first block of the hand-off within its stage
+      for (int h = 0; h < nh; ++h) {
+        const int kb0 = h * HB, nbh = min(HB, p.nkb - kb0);
+        const bool issue = (h % ISS) == mine;
+        bool ok = true;
+        if (issue) {
+          ok = mbar_wait(&full[st.i], st.ph);  // the stage's token tiles
+          ok = ok && mbar_wait(&afull[as.i], as.ph);
+          Ring u = ac;
+          const int k0 = (h / ISS) * UPH;  // this issuer's units so far
+#pragma unroll
+          for (int k = 0; k < UPH; ++k, u.next(NPI))
+            if (k0 + k >= NPI) ok = ok && mbar_wait(&accempty[mine * NPI + u.i], u.ph ^ 1u);
+        }
+        if (!ok) {
           set_status(p.status, kStatusTimeout);
           *abort_flag = 1;
           break;
         }
-        tc_fence_after();
-        uint8_t *st = stages + (size_t)s * p.stage_bytes;
-        const int nb = blocks_of(ks);
-        for (int j = 0; j < nb; ++j) {
-          const uint64_t adesc = umma_desc_sw128(st + j * kOpBytes);
-          const uint64_t bdesc = umma_desc_sw128(st + tok_off + j * p.a_bytes);
-          for (int g = 0; g < p.gps; ++g) {
-            const uint32_t d = tmem_d + (uint32_t)(((b * p.bps + j) * p.gps + g) * MPAD);
-            for (int kk = 0; kk < p.kpg; ++kk) {
-              const int kx = g * p.kpg + kk;  // 32-element step inside the 128-byte row
-              tc_mma_i8(d, adesc + (uint64_t)(2 * kx), bdesc + (uint64_t)(2 * kx), idesc, kk > 0 ? 1u : 0u);
+        if (issue) {
+          tc_fence_after();
+          const uint8_t *tok = stages + (size_t)st.i * p.stage_bytes + p.tok_off + j0 * TOK_BYTES;
+          const uint32_t at = tmem + (uint32_t)(as.i * HB * 32);
+          // accumulator units of this hand-off: this issuer's ac.i, ac.i + 1 (mod NPI)
+          const uint32_t d0 = tmem + (uint32_t)(SH::ACC0 + (mine * NPI + ac.i) * UCOLS);
+          const uint32_t d1 = tmem + (uint32_t)(SH::ACC0 + (mine * NPI + (ac.i + 1 == NPI ? 0 : ac.i + 1)) * UCOLS);
+#pragma unroll
+          for (int blk = 0; blk < HB; ++blk) {
+            if (blk < nbh) {
+              const uint64_t bdesc = umma_desc_sw128(tok + blk * TOK_BYTES);
+#pragma unroll
+              for (int kx = 0; kx < 4; ++kx) {  // K = 32 each: 8 A columns, 32 bytes of the token rows
+                const int g = blk * GPS + kx / KPG, u = g / UG, gi = g % UG;
+                const uint32_t d = (u == 0 ? d0 : d1) + (uint32_t)(gi * MPAD);
+                const uint32_t a = at + (uint32_t)(blk * 32 + 8 * kx);
+                if (kx % KPG == 0)
+                  tc_mma_i8_ts<false>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+                else
+                  tc_mma_i8_ts<true>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+              }
             }
           }
+          tc_commit(&mdone[h % kMD]);  // frees the A slot and hands the accumulators on
+#pragma unroll
+          for (int k = 0; k < UPH; ++k) ac.next(NPI);
         }
-        tc_commit(&empty[s]);
-        tc_commit(&mma_done[b]);
+        as.next(NAS);
+        j0 += HB;
+        if (j0 == kSB || h == nh - 1) {
+          tc_commit(&empty[st.i]);  // each issuer once per stage (after its own MMAs of it, if any)
+          st.next(p.nst);
+          j0 = 0;
+        }
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < kEpiWarp0) {
     // -------------------------------------------------------------- unpack --
-    const int r = threadIdx.x - 64;  // weight row of the tile
-    for (int ks = 0; ks < p.nks; ++ks) {
-      const int s = ks % p.nst;
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)(ks / p.nst) & 1u))) {
+    const int set = (warp - 2) >> 2;  // 0: even blocks, 1: odd blocks
+    const int quarter = warp & 3;     // TMEM lanes 32 * quarter ..
+    const int r = quarter * 32 + lane;  // weight row of the tile
+    const bool live = r < p.tile_rows;
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    bool stop = false;
+    Ring st;
+    for (int ks = 0; ks < p.nks && !stop; ++ks, st.next(p.nst)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[st.i], st.ph))) {
         if (lane == 0) set_status(p.status, kStatusTimeout);
         break;
       }
-      uint8_t *st = stages + (size_t)s * p.stage_bytes;
+      uint8_t *stg = stages + (size_t)st.i * p.stage_bytes;
       const int nb = blocks_of(ks);
-      if (r < p.tile_rows) {
-        for (int j = 0; j < nb; ++j) {
-          const uint8_t *src = st + pk_off + j * p.pk_bytes + (size_t)r * kPacked;
-          uint8_t *dst = st + j * kOpBytes + (size_t)r * kStageK;
-          // 16 packed bytes = 32 weights = two 16-byte output chunks.  The
-          // chunk order rotates with lane / 8: packed rows are 64 bytes apart,
-          // so the 32 lanes reading chunk q together would hit 8 of the 32
-          // banks (16-way conflicts); rotated they cover all banks, and each
-          // group of 8 rows keeps one chunk, so the swizzled 16-byte stores
-          // below stay conflict-free too.
-#pragma unroll
-          for (int q0 = 0; q0 < 4; ++q0) {
-            const int q = (q0 + (lane >> 3)) & 3;
-            const uint4 v = lds128(src + 16 * q);
-            uint32_t o[8];
-            unpack8x16(v.x, o[0], o[1]);
-            unpack8x16(v.y, o[2], o[3]);
-            unpack8x16(v.z, o[4], o[5]);
-            unpack8x16(v.w, o[6], o[7]);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int c = 2 * q + h;  // 16-byte chunk of the 128-byte row, swizzled by the row within its 8
-              *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) << 4)) =
-                  make_uint4(o[4 * h], o[4 * h + 1], o[4 * h + 2], o[4 * h + 3]);
-            }
-          }
+      // HB = 2: both sets write the two blocks of each hand-off into one slot
+      // (and both arrive, even where the last hand-off has one block);
+      // HB = 1: each set its own blocks, one slot each
+      for (int j0 = (HB == 2 ? 0 : set); j0 < nb; j0 += 2) {
+        const int j = HB == 2 ? j0 + set : j0;  // this warp's block of the stage
+        const int h = (ks * kSB + j0) / HB;     // hand-off: its A slot h % NAS, used for the (h / NAS)-th time
+        const int slot = h % NAS;
+        // the slot's previous hand-off (h - NAS) must have been read by its MMAs
+        if (h >= NAS &&
+            !__all_sync(0xffffffffu, mbar_wait(&mdone[(h - NAS) % kMD], (uint32_t)((h - NAS) / kMD) & 1u))) {
+          if (lane == 0) set_status(p.status, kStatusTimeout);
+          stop = true;
+          break;
         }
+        if (j < nb) {
+          // this block's token tile into the A operand's k order (its MMAs
+          // wait for this set's arrival below), generic stores made visible
+          // to the tensor core's reads
+          uint8_t *tok = stg + p.tok_off + j * TOK_BYTES;
+#pragma unroll
+          for (int q = 0; q < TOK_BYTES / 8 / 128; ++q) {
+            uint2 *u = reinterpret_cast<uint2 *>(tok) + quarter * 32 + lane + 128 * q;
+            const uint2 x = *u;
+            *u = make_uint2(prmt(x.x, x.y, 0x6420), prmt(x.x, x.y, 0x7531));
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          tc_fence_after();
+          uint32_t o[32];
+          if (live) {
+            // block j is half (j & 1) of packed box j / 2: logical 16-byte
+            // chunks 4(j & 1) .. +3 of the row, stored at chunk ^ (row & 7)
+            const uint8_t *rowp = stg + (j >> 1) * p.box_bytes + r * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int c = (j & 1) * 4 + q;
+              const uint4 v = lds128(rowp + ((c ^ (r & 7)) << 4));
+              unpack8x16(v.x, o[8 * q + 0], o[8 * q + 1]);
+              unpack8x16(v.y, o[8 * q + 2], o[8 * q + 3]);
+              unpack8x16(v.z, o[8 * q + 4], o[8 * q + 5]);
+              unpack8x16(v.w, o[8 * q + 6], o[8 * q + 7]);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = 0u;
+          }
+          // column c of the block holds k = 4c .. 4c + 3
+          tc_st32(lane_base + (uint32_t)(slot * HB * 32 + (HB == 2 ? set : 0) * 32), o);
+          tc_wait_st();
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[slot]);
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA operand reads
       __syncwarp();
-      if (lane == 0) mbar_arrive(&unpacked[s]);
+      if (lane == 0) mbar_arrive(&empty[st.i]);  // this warp is done with the stage's packed boxes
     }
   } else {
     // ------------------------------------------------------------ epilogue --
+    // EW / 4 sets of four warps (one per TMEM lane quarter), each for its
+    // share of the tokens: per token the groups are summed in order either way
     const int quarter = warp & 3;
+    const int half = (warp - kEpiWarp0) >> 2;  // token set
     const int r = quarter * 32 + lane;
     const int n = row0 + r;
     const bool row_ok = r < p.tile_rows && n < p.n;
+    constexpr int TPW = MR / (EW / 4);  // tokens of this warp: half * TPW ..
+    constexpr int PIECE = TPW % 16 == 0 ? 16 : TPW % 8 == 0 ? 8 : 4;  // accumulator columns per tcgen05.ld
+    constexpr int PPG = TPW / PIECE;                                  // loads per group
+    constexpr int NPC = UG * PPG;                                     // loads per unit
+    constexpr int CAP = TPW >= 16 ? 32 : 64;                          // registers of loads in flight
+    constexpr int BP = NPC * PIECE <= CAP ? NPC : CAP / PIECE;        // loads per wait
     pdl_wait();
-    float acc[MPAD];
+    float acc[TPW];
 #pragma unroll
-    for (int t = 0; t < MPAD; ++t) acc[t] = 0.0f;
+    for (int t = 0; t < TPW; ++t) acc[t] = 0.0f;
     bool stop = false;
-    const uint32_t lane_base = tmem_d + ((uint32_t)(quarter * 32) << 16);
-    const int gst = p.bps * p.gps;  // group accumulators per full stage
-    for (int ks = 0; ks < p.nks && !stop; ++ks) {
-      const int b = ks % p.nbuf;
-      const int bi = ks / p.spb, sb = bi % kScaleRing;
+    const uint32_t lane_base =
+        tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(SH::ACC0 + half * TPW);
+    Ring er[ISS], sr;  // each issuer's accumulator units (taken in hand-off order); scale box ring
+    int j0 = 0, sk = 0;  // first block of the hand-off in its stage; stage within the scale box
+    for (int h = 0; h < nh && !stop; ++h) {
+      const int nbh = min(HB, p.nkb - h * HB);
       bool ok = true;
-      if (ks % p.spb == 0) ok = mbar_wait(&sfull[sb], (uint32_t)(bi / kScaleRing) & 1u);
-      ok = ok && mbar_wait(&mma_done[b], (uint32_t)(ks / p.nbuf) & 1u);
+      if (j0 == 0 && sk == 0) ok = mbar_wait(&sfull[sr.i], sr.ph);
+      ok = ok && mbar_wait(&mdone[h % kMD], (uint32_t)(h / kMD) & 1u);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) set_status(p.status, kStatusTimeout);
         stop = true;
         break;
       }
       tc_fence_after();
-      const uint8_t *srow = sboxes + (size_t)sb * p.sbox_bytes + (size_t)r * p.sbox;
-      const int gbase = (ks % p.spb) * gst;  // this stage's first group inside the box row
-      const int ng = blocks_of(ks) * p.gps;  // groups computed in this stage
-      // The stage's group accumulators are contiguous TMEM columns
-      // ((b * bps + j) * gps + g) * MPAD: up to 64 of them are loaded before one wait.
-      constexpr int GPC = MPAD >= 48 ? 1 : 64 / MPAD;  // groups per load batch
-      for (int g0 = 0; g0 < ng; g0 += GPC) {
-        const int nvals = min(GPC, ng - g0) * MPAD;
-        const uint32_t col = lane_base + (uint32_t)((b * gst + g0) * MPAD);
-        uint32_t v0[16], v1[16], v2[16], v3[16];
-        tc_ld16_nowait(col, v0);
-        if (16 < nvals) tc_ld16_nowait(col + 16u, v1);
-        if (32 < nvals) tc_ld16_nowait(col + 32u, v2);
-        if (48 < nvals) tc_ld16_nowait(col + 48u, v3);
-        tc_wait_ld(v0, v1);
-        tc_wait_ld(v2, v3);  // nothing left to wait for: passes v2, v3 through the wait
-        float sc[GPC];
-        // the box holds tile_rows rows: lanes at and above them have no weight row
-        const int gi0 = gbase + g0;  // first scale index of the batch inside the box row
-        if (r < p.tile_rows && g0 + GPC <= ng && gi0 % GPC == 0 && (gi0 + GPC) * p.sbytes <= p.sbox) {
-          // the batch's scales in one vector load (rows are sbox bytes apart:
-          // one load per batch instead of GPC conflicting 2- or 4-byte loads)
-          if (p.sbytes == 2) {
-            uint32_t h[(GPC + 1) / 2];
-            if constexpr (GPC == 4) {
-              const uint2 t = *reinterpret_cast<const uint2 *>(srow + 2 * gi0);
-              h[0] = t.x;
-              h[1] = t.y;
-            } else if constexpr (GPC == 2) {
-              h[0] = *reinterpret_cast<const uint32_t *>(srow + 2 * gi0);
-            } else {
-              h[0] = *reinterpret_cast<const uint16_t *>(srow + 2 * gi0);
-            }
+      const uint8_t *srow = sboxes + (size_t)sr.i * p.sbox_bytes + (size_t)r * p.sbox;
+      Ring &ac = er[ISS == 2 ? (h & 1) : 0];
+      const int abase = (ISS == 2 ? (h & 1) : 0) * NPI;
 #pragma unroll
-            for (int gg = 0; gg < GPC; ++gg)
-              sc[gg] = __half2float(__ushort_as_half((unsigned short)(h[gg / 2] >> (16 * (gg & 1)))));
-          } else {
-            if constexpr (GPC == 4) {
-              const float4 t = *reinterpret_cast<const float4 *>(srow + 4 * gi0);
-              sc[0] = t.x;
-              sc[1] = t.y;
-              sc[2] = t.z;
-              sc[3] = t.w;
-            } else if constexpr (GPC == 2) {
-              const float2 t = *reinterpret_cast<const float2 *>(srow + 4 * gi0);
-              sc[0] = t.x;
-              sc[1] = t.y;
-            } else {
-              sc[0] = *reinterpret_cast<const float *>(srow + 4 * gi0);
+      for (int u = 0; u < UPH; ++u) {
+        const int ng = nbh * GPS - u * UG;  // groups of the unit that exist (the last hand-off may have one block)
+        const int slot = abase + ac.i;
+        const uint32_t col = lane_base + (uint32_t)(slot * UCOLS);
+#pragma unroll
+        for (int b0 = 0; b0 < NPC; b0 += BP) {
+          uint32_t v[BP][PIECE];
+#pragma unroll
+          for (int b = 0; b < BP; ++b) {
+            const int pc = b0 + b, g = pc / PPG, t0 = (pc % PPG) * PIECE;
+            if (pc < NPC && g < ng) {
+              if constexpr (PIECE == 4)
+                tc_ld4_nowait(col + (uint32_t)(g * MPAD + t0), v[b]);
+              else if constexpr (PIECE == 8)
+                tc_ld8_nowait(col + (uint32_t)(g * MPAD + t0), v[b]);
+              else
+                tc_ld16_nowait(col + (uint32_t)(g * MPAD + t0), v[b]);
             }
           }
-        } else {
+          // the unit's UG scales lie together in the box row (the box holds
+          // tile_rows rows: lanes at and above them read none); loaded while
+          // the accumulator loads are in flight
+          float sc[UG];
+          load_scales<UG>(srow, sk * (kSB * GPS) + j0 * GPS + u * UG, p.sbytes, r < p.tile_rows, sc);
 #pragma unroll
-          for (int gg = 0; gg < GPC; ++gg) {
-            const int gi = gi0 + gg;
-            sc[gg] = 0.0f;
-            if (r < p.tile_rows && g0 + gg < ng)
-              sc[gg] = p.sbytes == 2 ? __half2float(*reinterpret_cast<const __half *>(srow + 2 * gi))
-                                     : *reinterpret_cast<const float *>(srow + 4 * gi);
+          for (int b = 0; b < BP; ++b)
+            if (b0 + b < NPC && (b0 + b) / PPG < ng) tc_wait_ld_n<PIECE>(v[b]);
+#pragma unroll
+          for (int b = 0; b < BP; ++b) {
+            const int pc = b0 + b, g = pc / PPG, t0 = (pc % PPG) * PIECE;
+            if (pc < NPC && g < ng) {
+#pragma unroll
+              for (int i = 0; i < PIECE; ++i) acc[t0 + i] = fmaf(i2f_small(v[b][i]), sc[g], acc[t0 + i]);
+            }
           }
         }
-#pragma unroll
-        for (int gg = 0; gg < GPC; ++gg) sc[gg] = __fmul_rn(sc[gg], 0.0625f);  // the operand holds 16 x the weights
-#pragma unroll
-        for (int f = 0; f < GPC * MPAD && f < 64; ++f) {
-          const uint32_t u = f < 16 ? v0[f & 15] : f < 32 ? v1[f & 15] : f < 48 ? v2[f & 15] : v3[f & 15];
-          acc[f % MPAD] = fmaf((float)(int32_t)u, sc[f / MPAD], acc[f % MPAD]);
-        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accempty[slot]);
+        ac.next(NPI);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&tmem_free[b]);
-        if (ks % p.spb == p.spb - 1 || ks == p.nks - 1) mbar_arrive(&sempty[sb]);
+      j0 += HB;
+      if (j0 == kSB || h == nh - 1) {  // end of a stage
+        j0 = 0;
+        if (++sk == p.spb || h == nh - 1) {  // end of a scale box
+          if (lane == 0) mbar_arrive(&sempty[sr.i]);
+          sr.next(kScaleRing);
+          sk = 0;
+        }
       }
     }
     if (!stop && row_ok) {
       const float *__restrict__ sx = p.sx;
 #pragma unroll
-      for (int t = 0; t < MPAD; ++t)
-        if (t < p.m) p.y[(int64_t)t * p.ldy + n] = __fmul_rn(acc[t], sx[t]);
+      for (int t = 0; t < TPW; ++t) {
+        const int tt = half * TPW + t;
+        if (tt < p.m) p.y[(int64_t)tt * p.ldy + n] = __fmul_rn(acc[t], sx[tt]);
+      }
     }
   }
 
@@ -381,8 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(p.tmem_cols)
-                 : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
 }
 
@@ -392,19 +563,20 @@ bool make_plain_map(CUtensorMap *map, const void *base, int64_t rows, int64_t ro
   return make_map(map, base, rows, row_bytes, ld, box_rows, box_cols, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-template <int MPAD>
-cudaError_t launch_mpad(const CUtensorMap &mw, const CUtensorMap &ma, const CUtensorMap &ms, const W4GemmParams &p,
-                        int grid, size_t smem, cudaStream_t stream, int device) {
+template <int MPAD, int MR, int KPG>
+cudaError_t launch_one(const CUtensorMap &mw, const CUtensorMap &ma, const CUtensorMap &ms, const W4GemmParams &p,
+                       int grid, size_t smem, cudaStream_t stream, int device) {
   static std::once_flag once[64];
   static cudaError_t err[64];
   std::call_once(once[device & 63], [&] {
-    err[device & 63] = cudaFuncSetAttribute(gemm_w4a8_tc_kernel<MPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    err[device & 63] = cudaFuncSetAttribute(gemm_w4a8_tc_kernel<MPAD, MR, KPG>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             device_props(device).smem_optin);
   });
   if (err[device & 63] != cudaSuccess) return err[device & 63];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(Roles<MR>::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -414,7 +586,20 @@ cudaError_t launch_mpad(const CUtensorMap &mw, const CUtensorMap &ma, const CUte
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, gemm_w4a8_tc_kernel<MPAD>, mw, ma, ms, p);
+  return cudaLaunchKernelEx(&cfg, gemm_w4a8_tc_kernel<MPAD, MR, KPG>, mw, ma, ms, p);
+}
+
+template <int KPG>
+cudaError_t launch_kpg(int mpad, int mr, const CUtensorMap &mw, const CUtensorMap &ma, const CUtensorMap &ms,
+                       const W4GemmParams &p, int grid, size_t smem, cudaStream_t stream, int device) {
+  switch (mpad) {
+    case 16:
+      return mr <= 8 ? launch_one<16, 8, KPG>(mw, ma, ms, p, grid, smem, stream, device)
+                     : launch_one<16, 16, KPG>(mw, ma, ms, p, grid, smem, stream, device);
+    case 32: return launch_one<32, 32, KPG>(mw, ma, ms, p, grid, smem, stream, device);
+    case 48: return launch_one<48, 48, KPG>(mw, ma, ms, p, grid, smem, stream, device);
+    default: return launch_one<64, 64, KPG>(mw, ma, ms, p, grid, smem, stream, device);
+  }
 }
 
 }  // namespace
@@ -440,59 +625,40 @@ cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int d
   p.k = (int32_t)a.k;
   p.status = a.status;
   const int mpad = (int)((a.m + 15) / 16 * 16);
-  p.nkb = (int32_t)((a.k + kStageK - 1) / kStageK);
-  p.gps = (int32_t)(kStageK / a.group) > 0 ? (int32_t)(kStageK / a.group) : 1;
-  p.kpg = (int32_t)(a.group / 32);
+  const int mr = a.m <= 8 ? 8 : mpad;
+  const int kpg = (int)(a.group / 32);
+  const int gps = 4 / kpg;
+  p.nkb = (int32_t)((a.k + kBlockK - 1) / kBlockK);
+  p.nks = (p.nkb + kSB - 1) / kSB;
   p.sbytes = a.stype == kScaleF16 ? 2 : 4;
   const int64_t slots = dp.sm_count;
   const int64_t waves = (a.n + slots * kRows - 1) / (slots * kRows);
   const int64_t even = (a.n + waves * slots - 1) / (waves * slots);
   p.tile_rows = (int32_t)std::min<int64_t>(kRows, (std::max<int64_t>(even, 16) + 15) / 16 * 16);
   const int grid = (int)((a.n + p.tile_rows - 1) / p.tile_rows);
-  p.a_bytes = mpad * kStageK;  // multiple of 2048
-  p.pk_bytes = (p.tile_rows * kPacked + 1023) / 1024 * 1024;
-  // Blocks per stage: KS_B200_W4GEMM_BLOCKS (1, 2 or 4), default 4, halved
-  // until TMEM holds two stages of group accumulators and shared memory two
-  // stages (fewer barrier round trips per MMA; each costs the MMA thread a
-  // few hundred cycles).
-  static const int env_bps = env_int("KS_B200_W4GEMM_BLOCKS", 4);
-  int bps = env_bps >= 4 ? 4 : env_bps >= 2 ? 2 : 1;
-  // a power of two, so the scale bytes per stage are too (TMA boxes and their
-  // x coordinates must be multiples of 16 bytes)
-  while (bps > p.nkb) bps /= 2;
-  auto sbox_of = [&](int bb) { return std::max(16, bb * p.gps * p.sbytes); };
-  auto sbox_bytes_of = [&](int bb) { return (p.tile_rows * sbox_of(bb) + 127) / 128 * 128; };
-  auto fixed_of = [&](int bb) { return 1024 /* alignment */ + kScaleRing * sbox_bytes_of(bb) + 512 /* barriers */; };
-  auto stage_of = [&](int bb) { return bb * (kOpBytes + p.a_bytes + p.pk_bytes); };
-  while (bps > 1 && (512 / (bps * p.gps * mpad) < 2 || (dp.smem_optin - fixed_of(bps)) / stage_of(bps) < 2)) bps /= 2;
-  p.bps = bps;
-  p.nks = (p.nkb + bps - 1) / bps;
-  p.sbox = sbox_of(bps);
-  p.spb = p.sbox / (bps * p.gps * p.sbytes);
-  p.sbox_bytes = sbox_bytes_of(bps);
-  p.stage_bytes = stage_of(bps);
-  const int per_buf = bps * p.gps * mpad;  // TMEM columns of one stage's group accumulators
-  p.nbuf = std::min(kMaxBufs, 512 / per_buf);
-  if (p.nbuf < 2) return cudaErrorNotSupported;
-  uint32_t cols = 32;
-  while (cols < (uint32_t)(p.nbuf * per_buf)) cols <<= 1;
-  p.tmem_cols = cols;
-  const int fixed = fixed_of(bps);
-  int nst = std::min({kMaxStagesW4, (dp.smem_optin - fixed) / p.stage_bytes, p.nks,
-                      std::max(1, env_int("KS_B200_W4GEMM_STAGES", kMaxStagesW4))});
+  p.box_bytes = p.tile_rows * 128;  // a multiple of 2048: every box and token tile stays 1024-aligned
+  p.tok_off = 2 * p.box_bytes;
+  p.stage_bytes = p.tok_off + kSB * mpad * kBlockK;
+  // scale boxes: a power of two bytes per row, at least 16 (TMA boxes and
+  // their x coordinates are multiples of 16 bytes)
+  p.sbox = std::max(16, kSB * gps * p.sbytes);
+  p.spb = p.sbox / (kSB * gps * p.sbytes);
+  p.sbox_bytes = (p.tile_rows * p.sbox + 127) / 128 * 128;
+  const int fixed = 1024 /* alignment */ + kScaleRing * p.sbox_bytes + 512 /* barriers */;
+  const int nst = std::min({kMaxStages, (dp.smem_optin - fixed) / p.stage_bytes, (int)p.nks,
+                            std::max(1, env_int("KS_B200_W4GEMM_STAGES", kMaxStages))});
   if (nst < 1) return cudaErrorNotSupported;
   p.nst = nst;
   CUtensorMap mw, ma, ms;
-  if (!make_plain_map(&mw, a.w, a.n, a.k / 2, a.wstride, kPacked, p.tile_rows) ||
+  if (!make_map(&mw, a.w, a.n, a.k / 2, a.wstride, p.tile_rows, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&ma, a.a, a.m, a.k, a.lda, mpad) ||
       !make_plain_map(&ms, a.s, a.n, a.k / a.group * p.sbytes, a.sstride * p.sbytes, p.sbox, p.tile_rows))
     return cudaErrorInvalidValue;
   const size_t smem = (size_t)fixed + (size_t)nst * p.stage_bytes;
-  switch (mpad) {
-    case 16: return launch_mpad<16>(mw, ma, ms, p, grid, smem, stream, device);
-    case 32: return launch_mpad<32>(mw, ma, ms, p, grid, smem, stream, device);
-    case 48: return launch_mpad<48>(mw, ma, ms, p, grid, smem, stream, device);
-    default: return launch_mpad<64>(mw, ma, ms, p, grid, smem, stream, device);
+  switch (kpg) {
+    case 1: return launch_kpg<1>(mpad, mr, mw, ma, ms, p, grid, smem, stream, device);
+    case 2: return launch_kpg<2>(mpad, mr, mw, ma, ms, p, grid, smem, stream, device);
+    default: return launch_kpg<4>(mpad, mr, mw, ma, ms, p, grid, smem, stream, device);
   }
 }
 
