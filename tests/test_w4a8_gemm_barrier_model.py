@@ -48,11 +48,13 @@ class Ring:
 
 
 
-def shape(MPAD, KPG, NA_k):
-    """The kernel's compile-time hand-off shape for Mpad tokens and G = 32 * KPG."""
+def shape(MPAD, KPG, NA_k, PK=False):
+    """The kernel's compile-time hand-off shape for Mpad tokens and G = 32 * KPG
+    (PK: at most 8 tokens, two groups per 16 accumulator columns)."""
     GPS = 4 // KPG; HB = 2 if GPS * MPAD <= 64 else 1; GPH = HB * GPS
-    UPH = 1 if GPH * MPAD <= 192 else 2; UG = GPH // UPH; UCOLS = UG * MPAD
-    NA = NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
+    GCOLS = 8 if PK else MPAD
+    UPH = 1 if GPH * GCOLS <= 192 else 2; UG = GPH // UPH; UCOLS = UG * GCOLS
+    NA = 4 if PK else NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
     NAS = NA // HB; NACC = min(8, (512 - NA * 32) // UCOLS)
     ISS = 2 if NACC >= 2 * UPH and NAS % 2 == 0 else 1
     NPI = NACC // ISS  # accumulator slots per issuer
@@ -60,10 +62,10 @@ def shape(MPAD, KPG, NA_k):
 
 
 
-def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False):
+def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=False):
     """One CTA over nkb 128-K blocks with an nst-stage ring; roles as
     generators that yield while they wait, stepped in random order."""
-    S = shape(MPAD, KPG, NA_k)
+    S = shape(MPAD, KPG, NA_k, PK)
     HB, UPH, NAS, ISS, NPI = S['HB'], S['UPH'], S['NAS'], S['ISS'], S['NPI']
     if shared_ring:  # the unsound form: two issuers waiting on one ring of units
         ISS, NPI = 2, S['NACC']
@@ -168,15 +170,16 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False):
 
 
 
-SHAPES = [(m, k, na) for m in (16, 32, 48, 64) for k in (1, 2, 4) for na in (4, 8)]
+SHAPES = [(m, k, na, False) for m in (16, 32, 48, 64) for k in (1, 2, 4) for na in (4, 8)] + \
+    [(16, k, 4, True) for k in (1, 2, 4)]
 
 
-@pytest.mark.parametrize("mpad,kpg,na", SHAPES)
-def test_protocol_hands_every_buffer_over_in_order(mpad, kpg, na):
+@pytest.mark.parametrize("mpad,kpg,na,pk", SHAPES)
+def test_protocol_hands_every_buffer_over_in_order(mpad, kpg, na, pk):
     for nkb in (1, 2, 3, 5, 33):
         for nst in (2, 3, 5):
             for seed in range(3):
-                run(MPAD=mpad, KPG=kpg, NA_k=na, nkb=nkb, nst=nst, seed=seed)
+                run(MPAD=mpad, KPG=kpg, NA_k=na, nkb=nkb, nst=nst, seed=seed, PK=pk)
 
 
 def test_shared_accumulator_ring_is_caught():
@@ -195,6 +198,7 @@ def test_shared_accumulator_ring_is_caught():
 def test_issuer_count_per_shape():
     """One issuer exactly where a hand-off's units need more than half of them."""
     assert shape(16, 1, 8)["ISS"] == 2 and shape(16, 1, 8)["NPI"] == 1
+    assert shape(16, 1, 4, PK=True)["ISS"] == 2 and shape(16, 1, 4, PK=True)["NPI"] == 3
     assert shape(64, 1, 8)["ISS"] == 1 and shape(64, 1, 8)["UPH"] == 2
     for m in (16, 32, 48, 64):
         for k in (1, 2, 4):

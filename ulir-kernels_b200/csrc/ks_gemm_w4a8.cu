@@ -116,15 +116,23 @@ __device__ __forceinline__ float i2f_small(uint32_t v) { return __int2float_rn((
 // units after the A slots, NAS A slots of HB blocks.  Fewer, larger hand-offs
 // matter: every barrier wait and commit of the MMA thread costs about a
 // hundred cycles while the unpack and epilogue warps share its scheduler.
-template <int MPAD, int KPG>
+//
+// PK (at most 8 tokens): two groups share one 16-column accumulator.  The
+// even group's MMAs read the token tile with the tokens in rows 0-7 (rows
+// 8-15 zero) and start fresh; the odd group's accumulate with the tokens
+// moved to rows 8-15 (rows 0-7 zero), so they fill columns 8-15 and add zero
+// to columns 0-7: 8 columns per group instead of 16, and a unit's groups in
+// consecutive columns.
+template <int MPAD, int KPG, bool PK>
 struct Shape {
   static constexpr int GPS = 4 / KPG;  // groups per block
   static constexpr int HB = GPS * MPAD <= 64 ? 2 : 1;
   static constexpr int GPH = HB * GPS;
-  static constexpr int UPH = GPH * MPAD <= 192 ? 1 : 2;
+  static constexpr int GCOLS = PK ? 8 : MPAD;  // accumulator columns per group
+  static constexpr int UPH = GPH * GCOLS <= 192 ? 1 : 2;
   static constexpr int UG = GPH / UPH;
-  static constexpr int UCOLS = UG * MPAD;
-  static constexpr int NA = (kTmemCols - kNA * 32) / UCOLS >= 2 ? kNA : 4;  // A blocks
+  static constexpr int UCOLS = UG * GCOLS;
+  static constexpr int NA = PK ? 4 : (kTmemCols - kNA * 32) / UCOLS >= 2 ? kNA : 4;  // A blocks
   static constexpr int NAS = NA / HB;
   static constexpr int ACC0 = NA * 32;  // accumulator columns start after the A slots
   static constexpr int NACC = (kTmemCols - ACC0) / UCOLS < kMaxAcc ? (kTmemCols - ACC0) / UCOLS : kMaxAcc;
@@ -136,6 +144,11 @@ struct Shape {
   static constexpr int ISS = NACC >= 2 * UPH && NAS % 2 == 0 ? 2 : 1;
   static constexpr int NPI = NACC / ISS;
   static_assert(NACC >= 2 && kSB % HB == 0, "two accumulator units at least; whole hand-offs per stage");
+  static_assert(!PK || (MPAD == 16 && HB == 2 && UPH == 1 && UG % 2 == 0), "pairs of groups per unit");
+  // token tile in shared memory: PK keeps 8 zero rows before the box, so the
+  // tile at row 8 has the tokens first and the tile at row 0 has them last
+  static constexpr int TOKB = (PK ? 24 : MPAD) * kBlockK;  // bytes per block
+  static constexpr int TOFF = PK ? 8 * kBlockK : 0;        // where TMA puts the box
 };
 
 // Epilogue warps -- two sets of four, each set half of the tokens -- and the
@@ -215,10 +228,12 @@ template <int MPAD, int MR, int KPG>
 __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
     gemm_w4a8_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_s, const W4GemmParams p) {
-  using SH = Shape<MPAD, KPG>;
+  using SH = Shape<MPAD, KPG, (MR <= 8)>;
+  constexpr bool PK = MR <= 8;
+  constexpr int TOKB = SH::TOKB, TOFF = SH::TOFF;
   constexpr int GPS = SH::GPS, HB = SH::HB, UPH = SH::UPH, UG = SH::UG, UCOLS = SH::UCOLS, NAS = SH::NAS,
                 NACC = SH::NACC, ISS = SH::ISS, NPI = SH::NPI;
-  constexpr int TOK_BYTES = MPAD * kBlockK;  // one token tile
+  constexpr int TOK_BYTES = MPAD * kBlockK;  // one token box
   constexpr int EW = Roles<MR>::EW;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -275,7 +290,7 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
     for (int b = 0; b < npk; ++b)
       tma_load_2d_hint(st + b * p.box_bytes, &tmap_w, (ks * kSB + 2 * b) * kBlockPacked, row0, &full[s], pol);
     for (int j = 0; j < nb; ++j)
-      tma_load_2d(st + p.tok_off + j * TOK_BYTES, &tmap_a, (ks * kSB + j) * kBlockK, 0, &full[s]);
+      tma_load_2d(st + p.tok_off + j * TOKB + TOFF, &tmap_a, (ks * kSB + j) * kBlockK, 0, &full[s]);
     ++issued;
     return true;
   };
@@ -284,6 +299,15 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if constexpr (PK) {
+    // the 8 zero rows before every token box, written once (TMA never does)
+    for (int i = threadIdx.x; i < p.nst * kSB * (TOFF / 16); i += blockDim.x) {
+      const int blk = i / (TOFF / 16), w = i % (TOFF / 16);
+      uint8_t *reg = stages + (size_t)(blk / kSB) * p.stage_bytes + p.tok_off + (blk % kSB) * TOKB;
+      reinterpret_cast<uint4 *>(reg)[w] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -343,7 +367,7 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
         }
         if (issue) {
           tc_fence_after();
-          const uint8_t *tok = stages + (size_t)st.i * p.stage_bytes + p.tok_off + j0 * TOK_BYTES;
+          const uint8_t *tok = stages + (size_t)st.i * p.stage_bytes + p.tok_off + j0 * TOKB;
           const uint32_t at = tmem + (uint32_t)(as.i * HB * 32);
           // accumulator units of this hand-off: this issuer's ac.i, ac.i + 1 (mod NPI)
           const uint32_t d0 = tmem + (uint32_t)(SH::ACC0 + (mine * NPI + ac.i) * UCOLS);
@@ -351,16 +375,29 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
 #pragma unroll
           for (int blk = 0; blk < HB; ++blk) {
             if (blk < nbh) {
-              const uint64_t bdesc = umma_desc_sw128(tok + blk * TOK_BYTES);
+              const uint8_t *reg = tok + blk * TOKB;
+              const uint64_t bdesc = umma_desc_sw128(reg + TOFF);  // tokens in the first rows
+              const uint64_t bodd = umma_desc_sw128(reg);          // PK: tokens in rows 8-15
 #pragma unroll
               for (int kx = 0; kx < 4; ++kx) {  // K = 32 each: 8 A columns, 32 bytes of the token rows
                 const int g = blk * GPS + kx / KPG, u = g / UG, gi = g % UG;
-                const uint32_t d = (u == 0 ? d0 : d1) + (uint32_t)(gi * MPAD);
                 const uint32_t a = at + (uint32_t)(blk * 32 + 8 * kx);
-                if (kx % KPG == 0)
-                  tc_mma_i8_ts<false>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
-                else
-                  tc_mma_i8_ts<true>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+                if constexpr (PK) {
+                  // groups 2q and 2q + 1 share the 16 columns at 16q
+                  const uint32_t d = (u == 0 ? d0 : d1) + (uint32_t)((gi / 2) * 16);
+                  if ((gi & 1) == 0 && kx % KPG == 0)
+                    tc_mma_i8_ts<false>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+                  else if ((gi & 1) == 0)
+                    tc_mma_i8_ts<true>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+                  else
+                    tc_mma_i8_ts<true>(d, a, bodd + (uint64_t)(2 * kx), idesc);
+                } else {
+                  const uint32_t d = (u == 0 ? d0 : d1) + (uint32_t)(gi * MPAD);
+                  if (kx % KPG == 0)
+                    tc_mma_i8_ts<false>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+                  else
+                    tc_mma_i8_ts<true>(d, a, bdesc + (uint64_t)(2 * kx), idesc);
+                }
               }
             }
           }
@@ -411,9 +448,10 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
           // this block's token tile into the A operand's k order (its MMAs
           // wait for this set's arrival below), generic stores made visible
           // to the tensor core's reads
-          uint8_t *tok = stg + p.tok_off + j * TOK_BYTES;
+          uint8_t *tok = stg + p.tok_off + j * TOKB + TOFF;
+          constexpr int TROWS = PK ? 8 : MPAD;  // rows that can hold tokens
 #pragma unroll
-          for (int q = 0; q < TOK_BYTES / 8 / 128; ++q) {
+          for (int q = 0; q < TROWS * kBlockK / 8 / 128; ++q) {
             uint2 *u = reinterpret_cast<uint2 *>(tok) + quarter * 32 + lane + 128 * q;
             const uint2 x = *u;
             *u = make_uint2(prmt(x.x, x.y, 0x6420), prmt(x.x, x.y, 0x7531));
@@ -451,6 +489,93 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue --
+    if constexpr (PK) {
+      // Two sets of four warps (one per TMEM lane quarter), each for half of
+      // a unit's groups: one load of its consecutive columns (8 tokens per
+      // group).  The two partial sums of a row are added once at the end.
+      const int quarter = warp & 3;
+      const int set = (warp - kEpiWarp0) >> 2;
+      const int r = quarter * 32 + lane;
+      const int n = row0 + r;
+      const bool row_ok = r < p.tile_rows && n < p.n;
+      constexpr int HG = UG / 2;    // groups of this set per unit
+      constexpr int CN = HG * 8;    // their columns
+      pdl_wait();
+      float acc[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[t] = 0.0f;
+      bool stop = false;
+      const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(SH::ACC0 + set * CN);
+      Ring er[ISS], sr;  // each issuer's accumulator units (in hand-off order); scale box ring
+      int j0 = 0, sk = 0;
+      for (int h = 0; h < nh && !stop; ++h) {
+        const int nbh = min(HB, p.nkb - h * HB);
+        bool ok = true;
+        if (j0 == 0 && sk == 0) ok = mbar_wait(&sfull[sr.i], sr.ph);
+        ok = ok && mbar_wait(&mdone[h % kMD], (uint32_t)(h / kMD) & 1u);
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) set_status(p.status, kStatusTimeout);
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        const int iss = ISS == 2 ? (h & 1) : 0;  // the issuer of this hand-off owns its units
+        Ring &ac = er[iss];
+        const int slot = iss * NPI + ac.i;
+        const int ng = nbh * GPS - set * HG;  // this set's groups that exist (the last hand-off may have one block)
+        uint32_t v[CN];
+        if (ng > 0) {
+          const uint32_t col = lane_base + (uint32_t)(slot * UCOLS);
+          if constexpr (CN == 32)
+            tc_ld32_nowait(col, v);
+          else if constexpr (CN == 16)
+            tc_ld16_nowait(col, v);
+          else
+            tc_ld8_nowait(col, v);
+        }
+        const uint8_t *srow = sboxes + (size_t)sr.i * p.sbox_bytes + (size_t)r * p.sbox;
+        float sc[HG];
+        load_scales<HG>(srow, sk * (kSB * GPS) + j0 * GPS + set * HG, p.sbytes, r < p.tile_rows, sc);
+        if (ng > 0) {
+          tc_wait_ld_n<CN>(v);
+#pragma unroll
+          for (int g = 0; g < HG; ++g)
+            if (g < ng) {
+#pragma unroll
+              for (int t = 0; t < 8; ++t) acc[t] = fmaf(i2f_small(v[g * 8 + t]), sc[g], acc[t]);
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&accempty[slot]);
+        ac.next(NPI);
+        j0 += HB;
+        if (j0 == kSB || h == nh - 1) {  // end of a stage
+          j0 = 0;
+          if (++sk == p.spb || h == nh - 1) {  // end of a scale box
+            if (lane == 0) mbar_arrive(&sempty[sr.i]);
+            sr.next(kScaleRing);
+            sk = 0;
+          }
+        }
+      }
+      // set 1's partial sums -> shared memory (the first ring stage: free
+      // once both sets have seen every hand-off's MMAs done) -> set 0 adds
+      // them and stores; both barriers are reached on every path
+      float *part = reinterpret_cast<float *>(stages);  // [8][128]
+      asm volatile("bar.sync 1, %0;" ::"n"(8 * 32) : "memory");
+      if (set == 1) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) part[t * kRows + r] = acc[t];
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(8 * 32) : "memory");
+      if (set == 0 && !stop && row_ok) {
+        const float *__restrict__ sx = p.sx;
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          if (t < p.m) p.y[(int64_t)t * p.ldy + n] = __fmul_rn(__fadd_rn(acc[t], part[t * kRows + r]), sx[t]);
+      }
+    } else {
     // EW / 4 sets of four warps (one per TMEM lane quarter), each for its
     // share of the tokens: per token the groups are summed in order either way
     const int quarter = warp & 3;
@@ -547,6 +672,7 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
         if (tt < p.m) p.y[(int64_t)tt * p.ldy + n] = __fmul_rn(acc[t], sx[tt]);
       }
     }
+    }
   }
 
   tc_fence_before();
@@ -638,7 +764,8 @@ cudaError_t launch_gemm_w4a8(const GemmW4A8Launch &a, cudaStream_t stream, int d
   const int grid = (int)((a.n + p.tile_rows - 1) / p.tile_rows);
   p.box_bytes = p.tile_rows * 128;  // a multiple of 2048: every box and token tile stays 1024-aligned
   p.tok_off = 2 * p.box_bytes;
-  p.stage_bytes = p.tok_off + kSB * mpad * kBlockK;
+  // token tiles: at most 8 tokens keep 8 zero rows before the box (paired accumulators)
+  p.stage_bytes = p.tok_off + kSB * (mr <= 8 ? 24 : mpad) * kBlockK;
   // scale boxes: a power of two bytes per row, at least 16 (TMA boxes and
   // their x coordinates are multiples of 16 bytes)
   p.sbox = std::max(16, kSB * gps * p.sbytes);

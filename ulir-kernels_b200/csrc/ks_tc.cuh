@@ -105,13 +105,34 @@ __device__ __forceinline__ void tc_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) 
                : "r"(taddr));
 }
 
+// 32 columns per lane.
+__device__ __forceinline__ void tc_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
 // Wait for the preceding tcgen05.ld, passing one 4-, 8- or 16-register array
 // through the asm (the other arrays of a batch go through further waits,
 // which then have nothing left to wait for).
 template <int N>
 __device__ __forceinline__ void tc_wait_ld_n(uint32_t (&a)[N]) {
-  static_assert(N == 4 || N == 8 || N == 16, "4, 8 or 16 registers");
-  if constexpr (N == 4) {
+  static_assert(N == 4 || N == 8 || N == 16 || N == 32, "4, 8, 16 or 32 registers");
+  if constexpr (N == 32) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                   "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]),
+                   "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]),
+                   "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]),
+                   "+r"(a[29]), "+r"(a[30]), "+r"(a[31])
+                 :
+                 : "memory");
+  } else if constexpr (N == 4) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]) : : "memory");
   } else if constexpr (N == 8) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
