@@ -54,7 +54,7 @@ def shape(MPAD, KPG, NA_k, PK=False):
     GPS = 4 // KPG; HB = 2 if GPS * MPAD <= 64 else 1; GPH = HB * GPS
     GCOLS = 8 if PK else MPAD
     UPH = 1 if GPH * GCOLS <= 192 else 2; UG = GPH // UPH; UCOLS = UG * GCOLS
-    NA = 4 if PK else NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
+    NA = NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
     NAS = NA // HB; NACC = min(8, (512 - NA * 32) // UCOLS)
     ISS = 2 if NACC >= 2 * UPH and NAS % 2 == 0 else 1
     NPI = NACC // ISS  # accumulator slots per issuer
@@ -171,7 +171,7 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
 
 
 SHAPES = [(m, k, na, False) for m in (16, 32, 48, 64) for k in (1, 2, 4) for na in (4, 8)] + \
-    [(16, k, 4, True) for k in (1, 2, 4)]
+    [(16, k, na, True) for k in (1, 2, 4) for na in (4, 8)]
 
 
 @pytest.mark.parametrize("mpad,kpg,na,pk", SHAPES)
@@ -198,7 +198,7 @@ def test_shared_accumulator_ring_is_caught():
 def test_issuer_count_per_shape():
     """One issuer exactly where a hand-off's units need more than half of them."""
     assert shape(16, 1, 8)["ISS"] == 2 and shape(16, 1, 8)["NPI"] == 1
-    assert shape(16, 1, 4, PK=True)["ISS"] == 2 and shape(16, 1, 4, PK=True)["NPI"] == 3
+    assert shape(16, 1, 8, PK=True)["ISS"] == 2 and shape(16, 1, 8, PK=True)["NPI"] == 2
     assert shape(64, 1, 8)["ISS"] == 1 and shape(64, 1, 8)["UPH"] == 2
     for m in (16, 32, 48, 64):
         for k in (1, 2, 4):

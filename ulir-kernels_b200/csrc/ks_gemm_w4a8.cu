@@ -62,10 +62,7 @@ constexpr int kBlockPacked = kBlockK / 2;      // packed bytes per row per block
 constexpr int kSB = 4;                         // blocks per ring stage (two 128-byte packed boxes)
 constexpr int kUnpackWarps = 8;                // two sets of four: even and odd blocks
 constexpr int kEpiWarp0 = 2 + kUnpackWarps;    // first epilogue warp
-#ifndef KS_W4_NA
-#define KS_W4_NA 8
-#endif
-constexpr int kNA = KS_W4_NA;                  // A blocks in TMEM (32 columns each), where the accumulators allow
+constexpr int kNA = 8;                         // A blocks in TMEM (32 columns each), where the accumulators allow
 constexpr int kTmemCols = 512;
 constexpr int kMaxStages = 8;
 constexpr int kMaxAcc = 8;
@@ -132,7 +129,7 @@ struct Shape {
   static constexpr int UPH = GPH * GCOLS <= 192 ? 1 : 2;
   static constexpr int UG = GPH / UPH;
   static constexpr int UCOLS = UG * GCOLS;
-  static constexpr int NA = PK ? 4 : (kTmemCols - kNA * 32) / UCOLS >= 2 ? kNA : 4;  // A blocks
+  static constexpr int NA = (kTmemCols - kNA * 32) / UCOLS >= 2 ? kNA : 4;  // A blocks
   static constexpr int NAS = NA / HB;
   static constexpr int ACC0 = NA * 32;  // accumulator columns start after the A slots
   static constexpr int NACC = (kTmemCols - ACC0) / UCOLS < kMaxAcc ? (kTmemCols - ACC0) / UCOLS : kMaxAcc;
