@@ -14,11 +14,12 @@
 // Swap-AB: weight rows fill the MMA's M = 128 (TMEM lanes), tokens its N
 // (padded to 16).  A CTA owns `tile_rows` weight rows (the same share for
 // every SM, a multiple of 16).  K runs in 128-element blocks (four MMAs of
-// K = 32), four blocks per ring stage.  The int4 weights are widened to int8
-// by the CUDA cores and written straight into tensor memory, which the MMA
-// reads as its A operand, so shared memory holds only what TMA brings in
-// (packed weights and tokens, ~37 KB per stage at M <= 16: five stages in
-// flight).  Roles:
+// K = 32), four blocks per ring stage, handed between the roles one or two
+// blocks at a time (Shape).  The int4 weights are widened to int8 by the CUDA
+// cores and written straight into tensor memory, which the MMA reads as its
+// A operand, so shared memory holds only what TMA brings in (packed weights
+// and tokens: about 40 KB per stage at M <= 16, five stages in flight).
+// Roles:
 //   warp 0      TMA: per stage two packed-weight boxes [tile_rows x 128 B]
 //               (128-byte swizzle: the unpack reads are conflict-free), four
 //               token tiles [Mpad x 128 B] (128-byte swizzle, the MMA's B
@@ -26,17 +27,26 @@
 //               [tile_rows x 16..64 B] into a ring of its own.  No multicast.
 //   warps 2-9   unpack, two sets of four (one warp per TMEM lane quarter;
 //               even and odd blocks): one weight row per lane, int4 -> int8
-//               holding 16 x the weight (shift + mask per 4 bytes, PRMT to
-//               interleave), tcgen05.st of the row's 32 columns into one of
-//               four A slots, tcgen05.wait::st, arrive.
-//   warp 1      MMA: per block four tcgen05.mma (A from the slot, B the token
-//               tile) into the groups' accumulator columns (fresh
-//               accumulators per group), all loops unrolled with
-//               compile-time accumulate flags; commits free the A slot, the
-//               stage (its tokens) and hand the accumulators on.
-//   warps 10-13 epilogue: tcgen05.ld a unit's group accumulators (one TMEM
-//               lane per weight row), acc[m] += f32(v) * (s[n, g] / 16),
-//               release the columns; at the end y = acc * sx.
+//               holding 16 x the weight (shift and mask; even k in one word,
+//               odd k in the next, the token tiles rewritten into the same k
+//               order), tcgen05.st of the row's 32 columns into an A slot,
+//               tcgen05.wait::st, arrive.
+//   warps 1, 18 MMA: one or two issuers (alternate hand-offs, each with its
+//               own accumulator units): per block four tcgen05.mma (A from
+//               the slot, B the token tile) into the groups' accumulator
+//               columns, loops unrolled with compile-time accumulate flags; a
+//               commit per hand-off frees the A slot and hands the
+//               accumulators on, one per stage frees the stage (its tokens).
+//   warps 10-17 epilogue, two sets of four: tcgen05.ld of a unit's group
+//               accumulators (one TMEM lane per weight row), acc[m] +=
+//               f32(v) * (s[n, g] / 16), release the columns; at the end
+//               y = acc * sx.  Each set takes half of the tokens, or, at most
+//               8 tokens (paired accumulators, Shape), half of the groups,
+//               the two partial sums added at the end.
+// Every barrier has one waiting role that takes its phases in order (a
+// parity wait is only sound while the barrier is at most one phase ahead of
+// or behind the waiter); tests/test_w4a8_gemm_barrier_model.py restates the
+// protocol and checks it under random interleavings.
 // Every wait is bounded (about one second); a timeout is recorded in the
 // status word, the waiting role stops, and the kernel runs to its end.
 

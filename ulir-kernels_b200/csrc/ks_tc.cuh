@@ -166,8 +166,9 @@ __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sy
 // MMA with the A operand in tensor memory (M = 128 lanes, one row per lane,
 // each 32-bit column holding four consecutive K elements, low byte first)
 // and B from shared memory.  ACC (accumulate into D) is a compile-time
-// constant: a run-time predicate made every MMA of a loop about three times
-// slower to issue.
+// constant: callers unroll their MMA loops with constant flags (a loop with
+// run-time bounds and a run-time predicate issued each MMA about three times
+// slower).
 template <bool ACC>
 __device__ __forceinline__ void tc_mma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc) {
   if constexpr (ACC) {
