@@ -31,12 +31,18 @@
 //     groups in registers from one load to the quantised bytes), then take
 //     pairs of rows from the ring and write the stage's outputs with its
 //     epilogue.  Between layers a fourth grid barrier hands the layer's
-//     output to the next layer's RMSNorm.
+//     output to the next layer's RMSNorm.  Only V (qkv[2h:3h]) feeds stage
+//     2, so V's rows stream first; a CTA arrives at the barrier that
+//     publishes V, then computes its Q rows, then waits -- and likewise
+//     computes its K rows between arriving at and waiting for the barrier
+//     that publishes h2: two of the four barriers per layer overlap rows
+//     that nothing waits for.
 // The ring (3 slots, ~195 KB per SM) holds about 4 us of HBM traffic.
 // Layer g of a call reads the previous layer's output and writes hbuf[g & 1]
 // (the last layer writes h_out); the intermediates (qkv, h2, gate, up, act)
 // are reused by every layer, each written after the barrier that ends the
-// previous layer's last read of it.
+// previous layer's last read of it (Q and K are read by nothing; a CTA
+// writes the same rows of them in every layer, in program order).
 //
 // Grid barrier: a 64-bit arrival counter in the workspace that only grows
 // (see grid_barrier); every spin is bounded (about one second) and on a
@@ -71,15 +77,21 @@ constexpr int kDecMaxSlots = 16;
 constexpr int kDecSlotTarget = 64 * 1024;  // bytes of one ring slot, about (fewer, longer copies)
 constexpr int kDecMaxLayers = 32;          // layers per launch (the parameter block holds their pointers)
 
-// One stage's shape as both the producer and the consumers walk it (the same
-// for every layer).  Matrix m of stage s is the layer's matrix kStageMat[s][m].
+// One segment of a layer -- rows [row_off, row_off + rows) of the layer's
+// matrix `mat` -- as both the producer and the consumers walk it (the same
+// for every layer).  Segments in stream order: V, Q (W_qkv rows 2h.., 0..),
+// O, K (W_qkv rows h..), gate, up, down.  V comes first because only V feeds
+// the layer's next stage; each CTA computes its Q rows after arriving at the
+// barrier that publishes V and its K rows after arriving at the one that
+// publishes h2, so those barriers' latency is spent on rows nobody waits for.
+constexpr int kSegs = 7;
+enum Seg { kSegV, kSegQ, kSegO, kSegK, kSegGate, kSegUp, kSegDown };
 struct DecStage {
-  int32_t count;  // matrices (2: gate and up)
-  int32_t rows, cols;
+  int32_t mat;                    // 0 qkv, 1 o, 2 gate, 3 up, 4 down
+  int32_t row_off, rows, cols;
   int32_t row_bytes, srow_bytes;  // dense rows: the row strides
   int32_t rps;                    // rows per ring slot (even)
 };
-__constant__ int kStageMat[4][2] = {{0, 0}, {1, 1}, {2, 3}, {4, 4}};
 
 // One layer's operands: packed int4 weights and f16 scale rows of qkv, o,
 // gate, up, down; the RMSNorm weight vectors.
@@ -90,8 +102,10 @@ struct DecLayer {
 };
 
 struct DecParams {
-  DecStage st[4];
-  int32_t nslots, slot_bytes, xbuf_bytes;
+  DecStage st[kSegs];
+  int32_t nslots, slot_bytes;
+  int32_t xbuf_bytes;   // the first input buffer (h columns: the inputs of V, Q, K and of gate, up)
+  int32_t xbuf2_bytes;  // the second (max(h, i) columns: the inputs of O and of down)
   int32_t gshift;    // log2(group / 32)
   int32_t inflight;  // slots issued and not yet landed, at most (0: up to the ring)
   int32_t layers;        // layers in this launch
@@ -170,16 +184,21 @@ __device__ __forceinline__ uint64_t barrier_base(const unsigned long long *count
   return v - v % per_launch;
 }
 
-// Every consumer thread of every CTA calls it, k = 0, 1, 2, ... in order.  All of
-// this CTA's consumer writes before it are visible to every consumer thread
-// of the grid after it.
+// Barrier k in two halves, every consumer thread of every CTA calling each,
+// k = 0, 1, 2, ... in order: all of this CTA's consumer writes before
+// grid_arrive(k) are visible to every consumer thread of the grid after
+// grid_wait(k).  Work between the halves overlaps the barrier's latency.
 // base: the launch's barrier base, in shared memory (read by thread 0 only).
-__device__ void grid_barrier(unsigned long long *count, const uint64_t *base, int k, int ctid, uint32_t *status) {
+__device__ void grid_arrive(unsigned long long *count, int ctid) {
   consumers_sync<kDecCW>();
   if (ctid == 0) {
     // release: this CTA's writes (ordered before it by the CTA barrier) are
     // visible to whoever acquires a count that includes this arrival
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(count) : "memory");
+  }
+}
+__device__ void grid_wait(unsigned long long *count, const uint64_t *base, int k, int ctid, uint32_t *status) {
+  if (ctid == 0) {
     const uint64_t target = *base + (uint64_t)(k + 1) * gridDim.x;
     const uint64_t t0 = globaltimer_ns();
     while ((int64_t)(ld_acquire_gpu_u64(count) - target) < 0) {
@@ -191,6 +210,10 @@ __device__ void grid_barrier(unsigned long long *count, const uint64_t *base, in
     }
   }
   consumers_sync<kDecCW>();  // the acquire above, passed on to every consumer thread
+}
+__device__ void grid_barrier(unsigned long long *count, const uint64_t *base, int k, int ctid, uint32_t *status) {
+  grid_arrive(count, ctid);
+  grid_wait(count, base, k, ctid, status);
 }
 
 // ---- input preparation in registers ---------------------------------------
@@ -362,9 +385,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   float *red = reinterpret_cast<float *>(smem + kBarBytes - 128);  // kDecCW floats
   uint32_t *amax_cta = reinterpret_cast<uint32_t *>(smem + kBarBytes - 192);  // this CTA's max|act| bits
   uint64_t *bar_base = reinterpret_cast<uint64_t *>(smem + kBarBytes - 256);  // the launch's barrier base
-  StageRows *geo = reinterpret_cast<StageRows *>(smem + kBarBytes - 512);  // 4 stages
-  uint8_t *xb = smem + kBarBytes;
-  uint8_t *ring = xb + P.xbuf_bytes;
+  StageRows *geo = reinterpret_cast<StageRows *>(smem + kBarBytes - 512);  // kSegs segments
+  uint8_t *xb = smem + kBarBytes;      // inputs of V, Q, K; of gate, up
+  uint8_t *xb2 = xb + P.xbuf_bytes;    // inputs of O; of down
+  uint8_t *ring = xb2 + P.xbuf2_bytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -373,7 +397,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
       mbar_init(&full[b], 1);
       mbar_init(&empty[b], kDecCW);
     }
-    for (int s = 0; s < 4; ++s) {
+    for (int s = 0; s < kSegs; ++s) {
       const DecStage &S = P.st[s];
       const int r0 = (int)((int64_t)blockIdx.x * S.rows / gridDim.x);
       const int r1 = (int)((int64_t)(blockIdx.x + 1) * S.rows / gridDim.x);
@@ -393,12 +417,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
       bool stop = false;
       for (int l = 0; l < P.layers && !stop; ++l) {
         const DecLayer &Ly = P.layer[l];
-        for (int s = 0; s < 4 && !stop; ++s) {
+        for (int s = 0; s < kSegs && !stop; ++s) {
           const DecStage &S = P.st[s];
           const StageRows G = geo[s];
-          for (int m = 0; m < S.count && !stop; ++m) {
-            const uint8_t *wm = Ly.w[kStageMat[s][m]] + (int64_t)G.r0 * S.row_bytes;
-            const uint8_t *sm = Ly.s[kStageMat[s][m]] + (int64_t)G.r0 * S.srow_bytes;
+          {
+            const uint8_t *wm = Ly.w[S.mat] + (int64_t)(S.row_off + G.r0) * S.row_bytes;
+            const uint8_t *sm = Ly.s[S.mat] + (int64_t)(S.row_off + G.r0) * S.srow_bytes;
             for (int lo = 0; lo < G.n; lo += S.rps, ++issued, rp.next(P.nslots)) {
               if (issued >= P.nslots && !mbar_wait(&empty[rp.b], rp.phase ^ 1u)) {
                 set_status(P.status, kStatusTimeout);
@@ -438,7 +462,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   // ------------------------------------------------------------- consumers --
   constexpr int JH = NH / 4, JI = NI / 4;  // 8-element groups per thread (NT = 512)
   const int ctid = threadIdx.x;
-  const int64_t h = P.st[1].rows, inter = P.st[2].rows;
+  const int64_t h = P.st[kSegO].rows, inter = P.st[kSegGate].rows;
   RingPos rp;
   int pair_base = 0, bk = 0;
   uint32_t mx = 0;
@@ -460,54 +484,62 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
       const int g = P.layer0 + l;
       return g == P.total_layers - 1 ? P.h_out : P.hbuf[g & 1];
     };
-    // stage 1: qkv = W_qkv . q(RMSNorm(h_in, norm1))
+    // V, then Q: x1 = q(RMSNorm(h_in, norm1)) in xb.  The barrier that
+    // publishes V is arrived at before Q and waited for after it.
     if (blockIdx.x == 0 && ctid == 0) atomicExch(P.amax, 0u);
     {
       float v[JH][8];
       load_groups<JH>(h_in(), (int)(h / 8), ctid, v);
       prep_groups<JH, kPrepRms>((int)h, v, nw, P.eps, 0.0f, xb, P.q[0], P.scales + 0, red, ctid);
-      consume_matrix<NH>(P.st[0], geo[0], PlainOut{P.qkv}, xb, P.gshift, ring, P.slot_bytes, P.nslots, full, empty,
-                         rp, pair_base, mx, stop, warp, lane, P.status);
     }
-    grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
+    consume_matrix<NH>(P.st[kSegV], geo[kSegV], PlainOut{P.qkv + 2 * h}, xb, P.gshift, ring, P.slot_bytes, P.nslots,
+                       full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
+    grid_arrive(P.bar_count, ctid);
+    consume_matrix<NH>(P.st[kSegQ], geo[kSegQ], PlainOut{P.qkv}, xb, P.gshift, ring, P.slot_bytes, P.nslots, full,
+                       empty, rp, pair_base, mx, stop, warp, lane, P.status);
+    grid_wait(P.bar_count, bar_base, bk++, ctid, P.status);
 
-    // stage 2: h2 = h_in + W_o . q(qkv[2h:3h])
+    // O: h2 = h_in + W_o . q(V), its input in xb2; then K on x1 (still in xb)
+    // between arriving at the barrier that publishes h2 and waiting for it
     {
       float v[JH][8];
       load_groups<JH>(P.qkv + 2 * h, (int)(h / 8), ctid, v);
-      prep_groups<JH, kPrepPlain>((int)h, v, nw, P.eps, 0.0f, xb, P.q[1], P.scales + 1, red, ctid);
-      consume_matrix<NH>(P.st[1], geo[1], ResidualOut{P.h2, h_in()}, xb, P.gshift, ring, P.slot_bytes, P.nslots,
-                         full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
+      prep_groups<JH, kPrepPlain>((int)h, v, nw, P.eps, 0.0f, xb2, P.q[1], P.scales + 1, red, ctid);
+      consume_matrix<NH>(P.st[kSegO], geo[kSegO], ResidualOut{P.h2, h_in()}, xb2, P.gshift, ring, P.slot_bytes,
+                         P.nslots, full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
     }
     load_groups<JH>(P.layer[l].norm2_w, (int)(h / 8), ctid, nw);
-    grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
+    grid_arrive(P.bar_count, ctid);
+    consume_matrix<NH>(P.st[kSegK], geo[kSegK], PlainOut{P.qkv + h}, xb, P.gshift, ring, P.slot_bytes, P.nslots,
+                       full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
+    grid_wait(P.bar_count, bar_base, bk++, ctid, P.status);  // also: every warp is done with x1
 
-    // stage 3: gate, up = W_g, W_u . q(RMSNorm(h2, norm2)); act = silu(gate) * up
+    // gate, up = W_g, W_u . q(RMSNorm(h2, norm2)) (input in xb); act = silu(gate) * up
     {
       float v[JH][8];
       load_groups<JH>(P.h2, (int)(h / 8), ctid, v);
       prep_groups<JH, kPrepRms>((int)h, v, nw, P.eps, 0.0f, xb, P.q[2], P.scales + 2, red, ctid);
-      consume_matrix<NH>(P.st[2], geo[2], PlainOut{P.gate}, xb, P.gshift, ring, P.slot_bytes, P.nslots, full, empty,
-                         rp, pair_base, mx, stop, warp, lane, P.status);
+      consume_matrix<NH>(P.st[kSegGate], geo[kSegGate], PlainOut{P.gate}, xb, P.gshift, ring, P.slot_bytes,
+                         P.nslots, full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
       consumers_sync<kDecCW>();  // gate rows (any warp) before the up pass reads them
-      consume_matrix<NH>(P.st[2], geo[2], SiluMulOut{P.up, P.gate, P.act, amax_cta}, xb, P.gshift, ring,
+      consume_matrix<NH>(P.st[kSegUp], geo[kSegUp], SiluMulOut{P.up, P.gate, P.act, amax_cta}, xb, P.gshift, ring,
                          P.slot_bytes, P.nslots, full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
       consumers_sync<kDecCW>();
       if (ctid == 0) {
         atomicMax(P.amax, *amax_cta);
-        *amax_cta = 0u;  // the next layer's stage 3 starts from zero
+        *amax_cta = 0u;  // the next layer's gate/up starts from zero
       }
     }
     grid_barrier(P.bar_count, bar_base, bk++, ctid, P.status);
 
-    // stage 4: h_out = h2 + W_d . q(act), scale from max|act| (atomics, read from L2)
+    // down: h_out = h2 + W_d . q(act), scale from max|act| (atomics, read from L2), input in xb2
     {
       float v[JI][8];
       const float amax = __uint_as_float(__ldcg(P.amax));
       load_groups<JI>(P.act, (int)(inter / 8), ctid, v);
-      prep_groups<JI, kPrepAmaxGiven>((int)inter, v, nw, P.eps, amax, xb, P.q[3], P.scales + 3, red, ctid);
-      consume_matrix<NI>(P.st[3], geo[3], ResidualOut{h_out(), P.h2}, xb, P.gshift, ring, P.slot_bytes, P.nslots,
-                         full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
+      prep_groups<JI, kPrepAmaxGiven>((int)inter, v, nw, P.eps, amax, xb2, P.q[3], P.scales + 3, red, ctid);
+      consume_matrix<NI>(P.st[kSegDown], geo[kSegDown], ResidualOut{h_out(), P.h2}, xb2, P.gshift, ring,
+                         P.slot_bytes, P.nslots, full, empty, rp, pair_base, mx, stop, warp, lane, P.status);
     }
     if (l + 1 < P.layers) {
       load_groups<JH>(P.layer[l + 1].norm1_w, (int)(h / 8), ctid, nw);
@@ -569,13 +601,17 @@ cudaError_t launch_decode_layers_persistent(const DecodeLayersArgs &a, cudaStrea
   const int NH = ncpl_for(h), NI = ncpl_for(i);
   if (!((NH == 4 && (NI == 12 || NI == 16)) || (NH == 8 && NI == 16))) return cudaErrorNotSupported;
   DecParams P{};
-  const int64_t rows[4] = {3 * h, h, i, h}, cols[4] = {h, h, h, i};
-  const int counts[4] = {1, 1, 2, 1};
+  // segments V, Q, O, K, gate, up, down: matrix, first row, rows, columns
+  const int mats[kSegs] = {0, 0, 1, 0, 2, 3, 4};
+  const int64_t offs[kSegs] = {2 * h, 0, 0, h, 0, 0, 0};
+  const int64_t rows[kSegs] = {h, h, h, h, i, i, h}, cols[kSegs] = {h, h, h, h, h, h, i};
   const int target = std::max(8, env_int("KS_B200_DECODE_SLOT_KB", kDecSlotTarget / 1024)) * 1024;
-  int slot = 0, xbuf = 0;
-  for (int s = 0; s < 4; ++s) {
+  int slot = 0, xbuf2 = 0;
+  const int xbuf = W4A8Op<__half, 4, false>::xbuf_bytes((int)(h / 32));
+  for (int s = 0; s < kSegs; ++s) {
     DecStage &S = P.st[s];
-    S.count = counts[s];
+    S.mat = mats[s];
+    S.row_off = (int32_t)offs[s];
     S.rows = (int32_t)rows[s];
     S.cols = (int32_t)cols[s];
     S.row_bytes = (int32_t)(cols[s] / 2);
@@ -584,7 +620,7 @@ cudaError_t launch_decode_layers_persistent(const DecodeLayersArgs &a, cudaStrea
     const int rt = S.row_bytes + S.srow_bytes;
     S.rps = std::max(2, (target / rt) & ~1);
     slot = std::max(slot, S.rps * rt);
-    xbuf = std::max(xbuf, W4A8Op<__half, 4, false>::xbuf_bytes((int)(cols[s] / 32)));
+    xbuf2 = std::max(xbuf2, W4A8Op<__half, 4, false>::xbuf_bytes((int)(cols[s] / 32)));
   }
   // 16-byte vector loads of the inputs, 16-byte bulk copies of the weights
   uintptr_t al = reinterpret_cast<uintptr_t>(a.h_in);
@@ -596,11 +632,12 @@ cudaError_t launch_decode_layers_persistent(const DecodeLayersArgs &a, cudaStrea
   if (al & 15u) return cudaErrorNotSupported;
   slot = (slot + 127) / 128 * 128;
   const DeviceProps &dp = device_props(device);
-  const int nslots = std::min(kDecMaxSlots, (dp.smem_optin - kBarBytes - xbuf) / slot);
+  const int nslots = std::min(kDecMaxSlots, (dp.smem_optin - kBarBytes - xbuf - xbuf2) / slot);
   if (nslots < 3) return cudaErrorNotSupported;
   P.nslots = nslots;
   P.slot_bytes = slot;
   P.xbuf_bytes = xbuf;
+  P.xbuf2_bytes = xbuf2;
   int gshift = 0;
   while ((int64_t(32) << gshift) < G) ++gshift;
   P.gshift = gshift;
@@ -621,7 +658,7 @@ cudaError_t launch_decode_layers_persistent(const DecodeLayersArgs &a, cudaStrea
   P.bar_count = reinterpret_cast<unsigned long long *>(a.amax + 32);  // +128 bytes, same 256-byte region
   for (int k = 0; k < 4; ++k) P.q[k] = a.q[k];
   P.status = a.status;
-  const size_t smem = (size_t)kBarBytes + xbuf + (size_t)nslots * slot;
+  const size_t smem = (size_t)kBarBytes + xbuf + xbuf2 + (size_t)nslots * slot;
   for (int l0 = 0; l0 < a.layers; l0 += kDecMaxLayers) {
     P.layer0 = l0;
     P.layers = std::min(kDecMaxLayers, a.layers - l0);

@@ -117,7 +117,7 @@ __device__ __forceinline__ void tc_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]
       : "r"(taddr));
 }
 
-// Wait for the preceding tcgen05.ld, passing one 4-, 8- or 16-register array
+// Wait for the preceding tcgen05.ld, passing one 4-, 8-, 16- or 32-register array
 // through the asm (the other arrays of a batch go through further waits,
 // which then have nothing left to wait for).
 template <int N>
