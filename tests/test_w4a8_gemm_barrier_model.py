@@ -51,7 +51,7 @@ class Ring:
 def shape(MPAD, KPG, NA_k, PK=False):
     """The kernel's compile-time hand-off shape for Mpad tokens and G = 32 * KPG
     (PK: at most 8 tokens, two groups per 16 accumulator columns)."""
-    GPS = 4 // KPG; HB = 2 if GPS * MPAD <= 64 else 1; GPH = HB * GPS
+    GPS = 4 // KPG; HB = 4 if PK else 2 if GPS * MPAD <= 64 else 1; GPH = HB * GPS
     GCOLS = 8 if PK else MPAD
     UPH = 1 if GPH * GCOLS <= 192 else 2; UG = GPH // UPH; UCOLS = UG * GCOLS
     NA = NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
@@ -72,7 +72,7 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
     kMD = 16; kSB = 4
     nks = (nkb + kSB - 1) // kSB; nh = (nkb + HB - 1) // HB
     full = [Bar(1) for _ in range(nst)]; empty = [Bar(8 + ISS) for _ in range(nst)]
-    afull = [Bar(4 * HB) for _ in range(NAS)]; mdone = [Bar(1) for _ in range(kMD)]
+    afull = [Bar(8 if HB >= 2 else 4) for _ in range(NAS)]; mdone = [Bar(1) for _ in range(kMD)]
     nslots = NPI if shared_ring else ISS * NPI
     accempty = [Bar(8) for _ in range(nslots)]
     stage_ver = [-1] * nst; aslot = [None] * NAS; acc = [None] * nslots
@@ -92,19 +92,21 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
             yield from wait(full[s], (ks // nst) & 1)
             assert stage_ver[s] == ks
             nb = blocks_of(ks)
-            j0 = 0 if HB == 2 else set_
+            j0 = 0 if HB >= 2 else set_
             while j0 < nb:
-                j = j0 + set_ if HB == 2 else j0
                 h = (ks * kSB + j0) // HB; slot = h % NAS
                 if h >= NAS: yield from wait(mdone[(h - NAS) % kMD], ((h - NAS) // kMD) & 1)
-                if j < nb:
-                    if q == 0:
-                        assert aslot[slot] is None or aslot[slot][1] == 'read' or aslot[slot][0] == h, ("A overwrite", h, aslot[slot])
-                        aslot[slot] = (h, 'writing')
-                    yield
-                    assert stage_ver[s] == ks
+                # this warp's blocks of the hand-off: j0 + set, j0 + set + 2, ... (HB >= 2)
+                for jj in (range(set_, HB, 2) if HB >= 2 else (0,)):
+                    j = j0 + jj
+                    if j < nb:
+                        if q == 0:
+                            assert aslot[slot] is None or aslot[slot][1] == 'read' or aslot[slot][0] == h, ("A overwrite", h, aslot[slot])
+                            aslot[slot] = (h, 'writing')
+                        yield
+                        assert stage_ver[s] == ks
                 afull[slot].arrive()
-                j0 += 2
+                j0 += HB if HB >= 2 else 2
             empty[s].arrive()
     def mma(mine):
         if mine >= ISS: return
@@ -198,7 +200,7 @@ def test_shared_accumulator_ring_is_caught():
 def test_issuer_count_per_shape():
     """One issuer exactly where a hand-off's units need more than half of them."""
     assert shape(16, 1, 8)["ISS"] == 2 and shape(16, 1, 8)["NPI"] == 1
-    assert shape(16, 1, 8, PK=True)["ISS"] == 2 and shape(16, 1, 8, PK=True)["NPI"] == 2
+    assert shape(16, 1, 8, PK=True)["ISS"] == 2 and shape(16, 1, 8, PK=True)["HB"] == 4
     assert shape(64, 1, 8)["ISS"] == 1 and shape(64, 1, 8)["UPH"] == 2
     for m in (16, 32, 48, 64):
         for k in (1, 2, 4):

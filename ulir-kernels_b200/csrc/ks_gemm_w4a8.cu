@@ -133,7 +133,7 @@ __device__ __forceinline__ float i2f_small(uint32_t v) { return __int2float_rn((
 template <int MPAD, int KPG, bool PK>
 struct Shape {
   static constexpr int GPS = 4 / KPG;  // groups per block
-  static constexpr int HB = GPS * MPAD <= 64 ? 2 : 1;
+  static constexpr int HB = PK ? 4 : GPS * MPAD <= 64 ? 2 : 1;
   static constexpr int GPH = HB * GPS;
   static constexpr int GCOLS = PK ? 8 : MPAD;  // accumulator columns per group
   static constexpr int UPH = GPH * GCOLS <= 192 ? 1 : 2;
@@ -151,7 +151,7 @@ struct Shape {
   static constexpr int ISS = NACC >= 2 * UPH && NAS % 2 == 0 ? 2 : 1;
   static constexpr int NPI = NACC / ISS;
   static_assert(NACC >= 2 && kSB % HB == 0, "two accumulator units at least; whole hand-offs per stage");
-  static_assert(!PK || (MPAD == 16 && HB == 2 && UPH == 1 && UG % 2 == 0), "pairs of groups per unit");
+  static_assert(!PK || (MPAD == 16 && HB == 4 && UPH == 1 && UG % 2 == 0), "pairs of groups per unit");
   // token tile in shared memory: PK keeps 8 zero rows before the box, so the
   // tile at row 8 has the tokens first and the tile at row 0 has them last
   static constexpr int TOKB = (PK ? 24 : MPAD) * kBlockK;  // bytes per block
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kUnpackWarps + ISS);  // eight unpack warps, one commit per MMA issuer
     }
-    for (int a = 0; a < NAS; ++a) mbar_init(&afull[a], 4 * HB);  // the warps of the sets writing the slot's blocks
+    for (int a = 0; a < NAS; ++a) mbar_init(&afull[a], HB >= 2 ? 8 : 4);  // the warps writing the slot's blocks
     for (int b = 0; b < kMD; ++b) mbar_init(&mdone[b], 1);
     for (int b = 0; b < NACC; ++b) mbar_init(&accempty[b], EW);
     for (int b = 0; b < kScaleRing; ++b) {
@@ -437,11 +437,10 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
       }
       uint8_t *stg = stages + (size_t)st.i * p.stage_bytes;
       const int nb = blocks_of(ks);
-      // HB = 2: both sets write the two blocks of each hand-off into one slot
-      // (and both arrive, even where the last hand-off has one block);
-      // HB = 1: each set its own blocks, one slot each
-      for (int j0 = (HB == 2 ? 0 : set); j0 < nb; j0 += 2) {
-        const int j = HB == 2 ? j0 + set : j0;  // this warp's block of the stage
+      // HB >= 2: both sets write the hand-off's blocks into one slot (set s
+      // the blocks j0 + s, j0 + s + 2, ...) and both arrive, even where the
+      // last hand-off has fewer blocks; HB = 1: each set its own blocks
+      for (int j0 = (HB >= 2 ? 0 : set); j0 < nb; j0 += (HB >= 2 ? HB : 2)) {
         const int h = (ks * kSB + j0) / HB;     // hand-off: its A slot h % NAS, used for the (h / NAS)-th time
         const int slot = h % NAS;
         // the slot's previous hand-off (h - NAS) must have been read by its MMAs
@@ -451,6 +450,9 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
           stop = true;
           break;
         }
+#pragma unroll
+        for (int jj = (HB >= 2 ? set : 0); jj < (HB >= 2 ? HB : 1); jj += 2) {
+        const int j = j0 + jj;  // this warp's block of the stage
         if (j < nb) {
           // this block's token tile into the A operand's k order (its MMAs
           // wait for this set's arrival below), generic stores made visible
@@ -484,9 +486,10 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
             for (int i = 0; i < 32; ++i) o[i] = 0u;
           }
           // column c of the block holds k = 4c .. 4c + 3
-          tc_st32(lane_base + (uint32_t)(slot * HB * 32 + (HB == 2 ? set : 0) * 32), o);
+          tc_st32(lane_base + (uint32_t)(slot * HB * 32 + jj * 32), o);
           tc_wait_st();
           tc_fence_before();
+        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[slot]);
@@ -507,6 +510,10 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
       const bool row_ok = r < p.tile_rows && n < p.n;
       constexpr int HG = UG / 2;    // groups of this set per unit
       constexpr int CN = HG * 8;    // their columns
+      constexpr int NL = CN > 32 ? CN / 32 : 1;  // loads (and waits) of up to 32 columns
+      constexpr int LC = CN / NL;
+      constexpr int GPL = LC / 8;                // groups per load
+      static_assert(CN % NL == 0 && (LC == 8 || LC == 16 || LC == 32), "column split");
       pdl_wait();
       float acc[8];
 #pragma unroll
@@ -530,27 +537,31 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
         Ring &ac = er[iss];
         const int slot = iss * NPI + ac.i;
         const int ng = nbh * GPS - set * HG;  // this set's groups that exist (the last hand-off may have one block)
-        uint32_t v[CN];
-        if (ng > 0) {
-          const uint32_t col = lane_base + (uint32_t)(slot * UCOLS);
-          if constexpr (CN == 32)
-            tc_ld32_nowait(col, v);
-          else if constexpr (CN == 16)
-            tc_ld16_nowait(col, v);
-          else
-            tc_ld8_nowait(col, v);
-        }
+        const uint32_t col = lane_base + (uint32_t)(slot * UCOLS);
         const uint8_t *srow = sboxes + (size_t)sr.i * p.sbox_bytes + (size_t)r * p.sbox;
         float sc[HG];
-        load_scales<HG>(srow, sk * (kSB * GPS) + j0 * GPS + set * HG, p.sbytes, r < p.tile_rows, sc);
-        if (ng > 0) {
-          tc_wait_ld_n<CN>(v);
 #pragma unroll
-          for (int g = 0; g < HG; ++g)
-            if (g < ng) {
+        for (int l = 0; l < NL; ++l) {
+          if (l * GPL < ng) {
+            uint32_t v[LC];
+            if constexpr (LC == 32)
+              tc_ld32_nowait(col + (uint32_t)(l * LC), v);
+            else if constexpr (LC == 16)
+              tc_ld16_nowait(col + (uint32_t)(l * LC), v);
+            else
+              tc_ld8_nowait(col + (uint32_t)(l * LC), v);
+            // the set's scales, loaded while the first load is in flight
+            if (l == 0) load_scales<HG>(srow, sk * (kSB * GPS) + j0 * GPS + set * HG, p.sbytes, r < p.tile_rows, sc);
+            tc_wait_ld_n<LC>(v);
 #pragma unroll
-              for (int t = 0; t < 8; ++t) acc[t] = fmaf(i2f_small(v[g * 8 + t]), sc[g], acc[t]);
+            for (int gg = 0; gg < GPL; ++gg) {
+              const int g = l * GPL + gg;
+              if (g < ng) {
+#pragma unroll
+                for (int t = 0; t < 8; ++t) acc[t] = fmaf(i2f_small(v[gg * 8 + t]), sc[g], acc[t]);
+              }
             }
+          }
         }
         tc_fence_before();
         __syncwarp();
