@@ -56,9 +56,10 @@ def shape(MPAD, KPG, NA_k, PK=False):
     UPH = 1 if GPH * GCOLS <= 192 else 2; UG = GPH // UPH; UCOLS = UG * GCOLS
     NA = NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
     NAS = NA // HB; NACC = min(8, (512 - NA * 32) // UCOLS)
-    ISS = 2 if NACC >= 2 * UPH and NAS % 2 == 0 else 1
-    NPI = NACC // ISS  # accumulator slots per issuer
-    return dict(GPS=GPS, HB=HB, UPH=UPH, NA=NA, NAS=NAS, NACC=NACC, ISS=ISS, NPI=NPI)
+    SPLIT = PK  # both issuers take every hand-off, half of its blocks each, one shared ring of units
+    ISS = 2 if SPLIT or (NACC >= 2 * UPH and NAS % 2 == 0) else 1
+    NPI = NACC if SPLIT else NACC // ISS  # units per ring
+    return dict(GPS=GPS, HB=HB, UPH=UPH, NA=NA, NAS=NAS, NACC=NACC, ISS=ISS, NPI=NPI, SPLIT=SPLIT)
 
 
 
@@ -67,13 +68,15 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
     generators that yield while they wait, stepped in random order."""
     S = shape(MPAD, KPG, NA_k, PK)
     HB, UPH, NAS, ISS, NPI = S['HB'], S['UPH'], S['NAS'], S['ISS'], S['NPI']
+    SPLIT = S['SPLIT']
     if shared_ring:  # the unsound form: two issuers waiting on one ring of units
         ISS, NPI = 2, S['NACC']
     kMD = 16; kSB = 4
     nks = (nkb + kSB - 1) // kSB; nh = (nkb + HB - 1) // HB
     full = [Bar(1) for _ in range(nst)]; empty = [Bar(8 + ISS) for _ in range(nst)]
-    afull = [Bar(8 if HB >= 2 else 4) for _ in range(NAS)]; mdone = [Bar(1) for _ in range(kMD)]
-    nslots = NPI if shared_ring else ISS * NPI
+    afull = [Bar(8 if HB >= 2 else 4) for _ in range(NAS)]; mdone = [Bar(2 if SPLIT else 1) for _ in range(kMD)]
+    halves = {}  # SPLIT: issuers done with a hand-off's MMAs
+    nslots = NPI if (shared_ring or SPLIT) else ISS * NPI
     accempty = [Bar(8) for _ in range(nslots)]
     stage_ver = [-1] * nst; aslot = [None] * NAS; acc = [None] * nslots
     def blocks_of(ks): return min(kSB, nkb - ks * kSB)
@@ -113,14 +116,14 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
         st, asr, ac = Ring(), Ring(), Ring()  # ac: this issuer's own unit ring
         j0 = 0
         for h in range(nh):
-            issue = (h % ISS) == mine
+            issue = SPLIT or (h % ISS) == mine
             if issue:
                 yield from wait(full[st.i], st.ph)
                 yield from wait(afull[asr.i], asr.ph)
                 if shared_ring:
                     ac = Ring(); [ac.next(NPI) for _ in range(h * UPH)]
-                u = ac.copy(); k0 = (h * UPH) if shared_ring else (h // ISS) * UPH
-                base = 0 if shared_ring else mine * NPI
+                u = ac.copy(); k0 = (h * UPH) if (shared_ring or SPLIT) else (h // ISS) * UPH
+                base = 0 if (shared_ring or SPLIT) else mine * NPI
                 for k in range(UPH):
                     if k0 + k >= NPI: yield from wait(accempty[base + u.i], u.ph ^ 1)
                     u.next(NPI)
@@ -129,14 +132,18 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
                 u = ac.copy()
                 for k in range(UPH):
                     sl = base + u.i
-                    assert acc[sl] is None or acc[sl][2] == 'read', ("acc overwrite", h, acc[sl])
+                    ok_prev = acc[sl] is None or acc[sl][2] == 'read' or (SPLIT and acc[sl][0] == h)
+                    assert ok_prev, ("acc overwrite", h, acc[sl])
                     acc[sl] = (h, k, 'computing', 0); u.next(NPI)
                 assert stage_ver[st.i] == (h * HB) // kSB
                 yield
-                aslot[asr.i] = (h, 'read')
-                u = ac.copy()
-                for k in range(UPH):
-                    sl = base + u.i; acc[sl] = (h, k, 'ready', 0); u.next(NPI)
+                n_done = halves.get(h, 0) + 1
+                halves[h] = n_done
+                if not SPLIT or n_done == 2:  # both halves of the hand-off issued and complete
+                    aslot[asr.i] = (h, 'read')
+                    u = ac.copy()
+                    for k in range(UPH):
+                        sl = base + u.i; acc[sl] = (h, k, 'ready', 0); u.next(NPI)
                 for k in range(UPH): ac.next(NPI)
                 mdone[h % kMD].arrive()
             asr.next(NAS)
@@ -147,7 +154,7 @@ def run(MPAD=64, KPG=1, nkb=32, nst=3, NA_k=8, seed=0, shared_ring=False, PK=Fal
         rings = [Ring() for _ in range(ISS)]
         for h in range(nh):
             yield from wait(mdone[h % kMD], (h // kMD) & 1)
-            i = 0 if shared_ring else h % ISS
+            i = 0 if (shared_ring or SPLIT) else h % ISS
             for u in range(UPH):
                 sl = i * NPI + rings[i].i
                 a = acc[sl]

@@ -148,8 +148,12 @@ struct Shape {
   // Every barrier then has one waiting role that takes its phases in order
   // (a parity wait is only sound while the barrier is at most one phase
   // ahead of or behind the waiter).
-  static constexpr int ISS = NACC >= 2 * UPH && NAS % 2 == 0 ? 2 : 1;
-  static constexpr int NPI = NACC / ISS;
+  // PK (whole-stage hand-offs): both issuers take every hand-off, issuer i
+  // its blocks 2i and 2i + 1, sharing one ring of accumulator units (every
+  // waiter still takes every phase in order)
+  static constexpr bool SPLIT = PK;
+  static constexpr int ISS = SPLIT ? 2 : NACC >= 2 * UPH && NAS % 2 == 0 ? 2 : 1;
+  static constexpr int NPI = SPLIT ? NACC : NACC / ISS;  // units per ring (one ring per issuer unless SPLIT)
   static_assert(NACC >= 2 && kSB % HB == 0, "two accumulator units at least; whole hand-offs per stage");
   static_assert(!PK || (MPAD == 16 && HB == 4 && UPH == 1 && UG % 2 == 0), "pairs of groups per unit");
   // token tile in shared memory: PK keeps 8 zero rows before the box, so the
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
       mbar_init(&empty[s], kUnpackWarps + ISS);  // eight unpack warps, one commit per MMA issuer
     }
     for (int a = 0; a < NAS; ++a) mbar_init(&afull[a], HB >= 2 ? 8 : 4);  // the warps writing the slot's blocks
-    for (int b = 0; b < kMD; ++b) mbar_init(&mdone[b], 1);
+    for (int b = 0; b < kMD; ++b) mbar_init(&mdone[b], SH::SPLIT ? 2 : 1);  // one commit per issuer of the hand-off
     for (int b = 0; b < NACC; ++b) mbar_init(&accempty[b], EW);
     for (int b = 0; b < kScaleRing; ++b) {
       mbar_init(&sfull[b], 1);
@@ -356,16 +360,17 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
       int j0 = 0;       // first block of the hand-off within its stage
       for (int h = 0; h < nh; ++h) {
         const int kb0 = h * HB, nbh = min(HB, p.nkb - kb0);
-        const bool issue = (h % ISS) == mine;
+        const bool issue = SH::SPLIT || (h % ISS) == mine;
         bool ok = true;
         if (issue) {
           ok = mbar_wait(&full[st.i], st.ph);  // the stage's token tiles
           ok = ok && mbar_wait(&afull[as.i], as.ph);
           Ring u = ac;
-          const int k0 = (h / ISS) * UPH;  // this issuer's units so far
+          const int k0 = (SH::SPLIT ? h : h / ISS) * UPH;  // this ring's units so far
+          const int rbase = SH::SPLIT ? 0 : mine * NPI;   // this issuer's ring
 #pragma unroll
           for (int k = 0; k < UPH; ++k, u.next(NPI))
-            if (k0 + k >= NPI) ok = ok && mbar_wait(&accempty[mine * NPI + u.i], u.ph ^ 1u);
+            if (k0 + k >= NPI) ok = ok && mbar_wait(&accempty[rbase + u.i], u.ph ^ 1u);
         }
         if (!ok) {
           set_status(p.status, kStatusTimeout);
@@ -376,12 +381,14 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
           tc_fence_after();
           const uint8_t *tok = stages + (size_t)st.i * p.stage_bytes + p.tok_off + j0 * TOKB;
           const uint32_t at = tmem + (uint32_t)(as.i * HB * 32);
-          // accumulator units of this hand-off: this issuer's ac.i, ac.i + 1 (mod NPI)
-          const uint32_t d0 = tmem + (uint32_t)(SH::ACC0 + (mine * NPI + ac.i) * UCOLS);
-          const uint32_t d1 = tmem + (uint32_t)(SH::ACC0 + (mine * NPI + (ac.i + 1 == NPI ? 0 : ac.i + 1)) * UCOLS);
+          // accumulator units of this hand-off: the ring's ac.i, ac.i + 1 (mod NPI)
+          const int rbase2 = SH::SPLIT ? 0 : mine * NPI;
+          const uint32_t d0 = tmem + (uint32_t)(SH::ACC0 + (rbase2 + ac.i) * UCOLS);
+          const uint32_t d1 = tmem + (uint32_t)(SH::ACC0 + (rbase2 + (ac.i + 1 == NPI ? 0 : ac.i + 1)) * UCOLS);
 #pragma unroll
           for (int blk = 0; blk < HB; ++blk) {
-            if (blk < nbh) {
+            // SPLIT: this issuer's blocks 2 * mine, 2 * mine + 1 only
+            if (blk < nbh && (!SH::SPLIT || blk / 2 == mine)) {
               const uint8_t *reg = tok + blk * TOKB;
               const uint64_t bdesc = umma_desc_sw128(reg + TOFF);  // tokens in the first rows
               const uint64_t bodd = umma_desc_sw128(reg);          // PK: tokens in rows 8-15
@@ -533,7 +540,7 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
           break;
         }
         tc_fence_after();
-        const int iss = ISS == 2 ? (h & 1) : 0;  // the issuer of this hand-off owns its units
+        const int iss = (ISS == 2 && !SH::SPLIT) ? (h & 1) : 0;  // the ring of this hand-off's units
         Ring &ac = er[iss];
         const int slot = iss * NPI + ac.i;
         const int ng = nbh * GPS - set * HG;  // this set's groups that exist (the last hand-off may have one block)
