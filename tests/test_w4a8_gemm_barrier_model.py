@@ -56,7 +56,7 @@ def shape(MPAD, KPG, NA_k, PK=False):
     UPH = 1 if GPH * GCOLS <= 192 else 2; UG = GPH // UPH; UCOLS = UG * GCOLS
     NA = NA_k if (512 - NA_k * 32) // UCOLS >= 2 else 4
     NAS = NA // HB; NACC = min(8, (512 - NA * 32) // UCOLS)
-    SPLIT = PK  # both issuers take every hand-off, half of its blocks each, one shared ring of units
+    SPLIT = MPAD == 16 and HB >= 2  # both issuers take every hand-off, half of its blocks each, one ring of units
     ISS = 2 if SPLIT or (NACC >= 2 * UPH and NAS % 2 == 0) else 1
     NPI = NACC if SPLIT else NACC // ISS  # units per ring
     return dict(GPS=GPS, HB=HB, UPH=UPH, NA=NA, NAS=NAS, NACC=NACC, ISS=ISS, NPI=NPI, SPLIT=SPLIT)
@@ -206,7 +206,8 @@ def test_shared_accumulator_ring_is_caught():
 
 def test_issuer_count_per_shape():
     """One issuer exactly where a hand-off's units need more than half of them."""
-    assert shape(16, 1, 8)["ISS"] == 2 and shape(16, 1, 8)["NPI"] == 1
+    assert shape(16, 1, 8)["ISS"] == 2 and shape(16, 1, 8)["SPLIT"] and shape(16, 1, 8)["NPI"] == 2
+    assert shape(32, 2, 8)["ISS"] == 2 and not shape(32, 2, 8)["SPLIT"] and shape(32, 2, 8)["NPI"] == 1
     assert shape(16, 1, 8, PK=True)["ISS"] == 2 and shape(16, 1, 8, PK=True)["HB"] == 4
     assert shape(64, 1, 8)["ISS"] == 1 and shape(64, 1, 8)["UPH"] == 2
     for m in (16, 32, 48, 64):

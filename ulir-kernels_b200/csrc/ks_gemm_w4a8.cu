@@ -148,10 +148,10 @@ struct Shape {
   // Every barrier then has one waiting role that takes its phases in order
   // (a parity wait is only sound while the barrier is at most one phase
   // ahead of or behind the waiter).
-  // PK (whole-stage hand-offs): both issuers take every hand-off, issuer i
-  // its blocks 2i and 2i + 1, sharing one ring of accumulator units (every
-  // waiter still takes every phase in order)
-  static constexpr bool SPLIT = PK;
+  // SPLIT (16-column tokens, hand-offs of 2 or 4 blocks): both issuers take
+  // every hand-off, issuer i the i-th half of its blocks, sharing one ring
+  // of accumulator units (every waiter still takes every phase in order)
+  static constexpr bool SPLIT = MPAD == 16 && HB >= 2;
   static constexpr int ISS = SPLIT ? 2 : NACC >= 2 * UPH && NAS % 2 == 0 ? 2 : 1;
   static constexpr int NPI = SPLIT ? NACC : NACC / ISS;  // units per ring (one ring per issuer unless SPLIT)
   static_assert(NACC >= 2 && kSB % HB == 0, "two accumulator units at least; whole hand-offs per stage");
@@ -387,8 +387,8 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
           const uint32_t d1 = tmem + (uint32_t)(SH::ACC0 + (rbase2 + (ac.i + 1 == NPI ? 0 : ac.i + 1)) * UCOLS);
 #pragma unroll
           for (int blk = 0; blk < HB; ++blk) {
-            // SPLIT: this issuer's blocks 2 * mine, 2 * mine + 1 only
-            if (blk < nbh && (!SH::SPLIT || blk / 2 == mine)) {
+            // SPLIT: this issuer's half of the blocks only
+            if (blk < nbh && (!SH::SPLIT || blk / (HB >= 2 ? HB / 2 : 1) == mine)) {
               const uint8_t *reg = tok + blk * TOKB;
               const uint64_t bdesc = umma_desc_sw128(reg + TOFF);  // tokens in the first rows
               const uint64_t bodd = umma_desc_sw128(reg);          // PK: tokens in rows 8-15
@@ -635,8 +635,8 @@ __global__ void __launch_bounds__(Roles<MR>::THREADS, 1)
       }
       tc_fence_after();
       const uint8_t *srow = sboxes + (size_t)sr.i * p.sbox_bytes + (size_t)r * p.sbox;
-      Ring &ac = er[ISS == 2 ? (h & 1) : 0];
-      const int abase = (ISS == 2 ? (h & 1) : 0) * NPI;
+      Ring &ac = er[(ISS == 2 && !SH::SPLIT) ? (h & 1) : 0];
+      const int abase = ((ISS == 2 && !SH::SPLIT) ? (h & 1) : 0) * NPI;
 #pragma unroll
       for (int u = 0; u < UPH; ++u) {
         const int ng = nbh * GPS - u * UG;  // groups of the unit that exist (the last hand-off may have one block)
