@@ -245,6 +245,31 @@ __device__ __forceinline__ void load_groups(const float *x, int ngroups, int cti
   }
 }
 
+// Sum / max over the consumer threads in a fixed order (bitwise the same in
+// every CTA) with one CTA barrier each: the two reductions of a preparation
+// use their own word arrays, and the preparation's closing barrier orders
+// every read of them before the next preparation writes them again.
+__device__ __forceinline__ float prep_sum(float v, float *red, int ctid) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((ctid & 31) == 0) red[ctid >> 5] = v;
+  consumers_sync<kDecCW>();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kDecCW; ++w) t += red[w];
+  return t;
+}
+__device__ __forceinline__ float prep_max(float v, float *red, int ctid) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((ctid & 31) == 0) red[ctid >> 5] = v;
+  consumers_sync<kDecCW>();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kDecCW; ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
 enum PrepMode { kPrepPlain, kPrepRms, kPrepAmaxGiven };
 
 // v: the thread's groups (loaded); nw: RMSNorm weights of the same groups
@@ -261,7 +286,7 @@ __device__ __forceinline__ void prep_groups(int K, float (&v)[J][8], const float
     for (int j = 0; j < J; ++j)
 #pragma unroll
       for (int t = 0; t < 8; ++t) ss = __fadd_rn(ss, __fmul_rn(v[j][t], v[j][t]));
-    ss = consumers_sum<kDecCW>(ss, red, ctid);
+    ss = prep_sum(ss, red, ctid);
     const float scale = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
 #pragma unroll
     for (int j = 0; j < J; ++j)
@@ -277,7 +302,7 @@ __device__ __forceinline__ void prep_groups(int K, float (&v)[J][8], const float
     for (int j = 0; j < J; ++j)
 #pragma unroll
       for (int t = 0; t < 8; ++t) m = fmaxf(m, fabsf(v[j][t]));
-    amax = consumers_max<kDecCW>(m, red, ctid);
+    amax = prep_max(m, red + kDecCW, ctid);
   }
   const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
   const float inv = __fdiv_rn(1.0f, s);
@@ -382,7 +407,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(const __gr
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
   uint64_t *empty = full + P.nslots;
-  float *red = reinterpret_cast<float *>(smem + kBarBytes - 128);  // kDecCW floats
+  float *red = reinterpret_cast<float *>(smem + kBarBytes - 128);  // 2 x kDecCW floats (sum, max)
   uint32_t *amax_cta = reinterpret_cast<uint32_t *>(smem + kBarBytes - 192);  // this CTA's max|act| bits
   uint64_t *bar_base = reinterpret_cast<uint64_t *>(smem + kBarBytes - 256);  // the launch's barrier base
   StageRows *geo = reinterpret_cast<StageRows *>(smem + kBarBytes - 512);  // kSegs segments

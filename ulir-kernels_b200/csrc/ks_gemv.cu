@@ -394,8 +394,10 @@ int ilog2_exact(int64_t v) {
 // Fill the ring geometry for one configuration (single or batch); false if
 // the rows are too long to stage.
 // l2_ahead: L2 prefetch distance in stages (measured best on B200: W4A8 1
-// single / 2 batched, INT8 1 single / 0 batched; farther prefetches compete
-// with the ring's own copies).
+// single / 0 batched, INT8 1 single / 0 batched; farther prefetches compete
+// with the ring's own copies).  Batched W4A8 without the prefetch, per GEMV:
+// 3.92 against 3.95 us at 11008 x 4096 G32, 16.99 against 17.22 us at
+// 28672 x 8192 G128, 5.39 against 5.40 at 7168 x 8192.
 // peer: the launch gathers its outputs by peer stores and stages each
 // matrix's rows in two shared-memory buffers of rows_cta_max floats.
 bool plan_stream(StreamGeom &g, int64_t rows, int row_bytes, int srow_bytes, int xbuf_bytes, int sm_count,
@@ -511,7 +513,7 @@ W4A8Plan plan_w4a8(const W4A8Launch &a, int device, bool batch, bool peer = fals
   const int xbuf = ((chunks * 36 + 4 + 127) / 128) * 128;
   StreamGeom g{};
   if (!plan_stream(g, a.rows, (int)(a.cols / 2), (int)(groups * ssize), xbuf, device_props(device).sm_count,
-                   batch, batch ? 16 : 8, batch ? 2 : 1, peer))
+                   batch, batch ? 16 : 8, batch ? 0 : 1, peer))
     return P;
   g.wstride = a.wstride;
   g.sstride = a.sstride * ssize;
@@ -704,12 +706,30 @@ int i8_path(const I8Launch &a) {
   return (aligned16(a.w) && plan_i8(a, dev, false).fast) ? 1 : 0;
 }
 
+// A single GEMV whose rows give each CTA at least this many bytes to stream
+// takes the one-CTA-per-SM geometry with the deep (~200 KB) ring instead of
+// the two-CTA form (~100 KB each, so that the next launch of a chain can
+// start beside it).  Measured on B200, W4A8 G128 f16, one launch per matrix
+// in a dependent chain: 28672 x 8192 (800 KB per CTA) 21.4 against 25.8 us,
+// 7168 x 8192 (207 KB) 8.53 against 8.72 us; 11008 x 4096 G32 (171 KB)
+// 7.56 against 7.37 us, so it keeps the two-CTA form.
+constexpr int64_t kDeepSingleBytes = 192 * 1024;
+
 cudaError_t launch_w4a8(const W4A8Launch &a, cudaStream_t stream, int device) {
   W4A8Plan P;
   if (aligned16(a.w) && aligned16(a.s)) P = plan_w4a8(a, device, false);
   if (!P.fast) return launch_w4a8_generic(a, stream, device);
   GemvItems items{};
   items.it[0] = GemvItem{a.x, a.w, reinterpret_cast<const uint8_t *>(a.s), a.y};
+  const int64_t cta_bytes = (P.g.rows + P.g.n_cta - 1) / P.g.n_cta * (int64_t)(P.g.row_bytes + P.g.srow_bytes);
+  if (cta_bytes >= kDeepSingleBytes) {
+    W4A8Plan Q = plan_w4a8(a, device, true);
+    if (Q.fast) {
+      Q.g.count = 1;
+      Q.g.x_al16 = aligned16(a.x);
+      return launch_w4a8_cw<16>(Q, a.stype, items, stream, device);
+    }
+  }
   P.g.count = 1;
   P.g.x_al16 = aligned16(a.x);
   return launch_w4a8_cw<8>(P, a.stype, items, stream, device);
@@ -819,6 +839,14 @@ cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b
   if (!batch_aligned(b, true)) return cudaErrorInvalidValue;
   W4A8Plan P = plan_w4a8(shape, device, b.count > 1, /*peer=*/true);
   if (!P.fast) return cudaErrorInvalidValue;
+  bool wide = b.count > 1;  // the one-CTA-per-SM geometry (as launch_w4a8 picks it for a long single GEMV)
+  if (!wide && (P.g.rows + P.g.n_cta - 1) / P.g.n_cta * (int64_t)(P.g.row_bytes + P.g.srow_bytes) >= kDeepSingleBytes) {
+    const W4A8Plan D = plan_w4a8(shape, device, true, /*peer=*/true);
+    if (D.fast) {
+      P = D;
+      wide = true;
+    }
+  }
   for (int i0 = 0; i0 < b.count; i0 += kMaxItems) {
     const int n = std::min(kMaxItems, b.count - i0);
     GemvItems items{};
@@ -835,8 +863,8 @@ cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b
     W4A8Plan Q = P;
     Q.g.count = n;
     Q.g.x_al16 = batch_x_aligned(b, i0, n);
-    cudaError_t e = b.count > 1 ? launch_w4a8_cw<16>(Q, shape.stype, items, stream, device)
-                                : launch_w4a8_cw<8>(Q, shape.stype, items, stream, device);
+    cudaError_t e = wide ? launch_w4a8_cw<16>(Q, shape.stype, items, stream, device)
+                         : launch_w4a8_cw<8>(Q, shape.stype, items, stream, device);
     if (e != cudaSuccess) return e;
     *signals_per_rank += (uint32_t)Q.g.n_cta;
   }
