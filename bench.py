@@ -62,9 +62,9 @@ SEED = 20261201
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of the batched W4A8 kernel on
-# this workload, per GEMV (one ncu launch = 64 GEMVs: 1,623,529,984 +
-# 6,268,160 bytes), from the capture summarised under profiles/.
-NCU_TRAFFIC_PER_GEMV = (1_623_529_984 + 6_268_160) // 64
+# this workload, per GEMV (one ncu launch = 64 GEMVs: 1,623,533,056 +
+# 5,308,672 bytes), from the capture summarised under profiles/.
+NCU_TRAFFIC_PER_GEMV = (1_623_533_056 + 5_308_672) // 64
 
 
 def gemv_bytes(rows=ROWS, cols=COLS, group=GROUP, scale_bytes=2) -> int:
