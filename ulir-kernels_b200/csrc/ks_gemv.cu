@@ -839,14 +839,7 @@ cudaError_t launch_w4a8_batch_gather(const W4A8Launch &shape, const GemvBatch &b
   if (!batch_aligned(b, true)) return cudaErrorInvalidValue;
   W4A8Plan P = plan_w4a8(shape, device, b.count > 1, /*peer=*/true);
   if (!P.fast) return cudaErrorInvalidValue;
-  bool wide = b.count > 1;  // the one-CTA-per-SM geometry (as launch_w4a8 picks it for a long single GEMV)
-  if (!wide && (P.g.rows + P.g.n_cta - 1) / P.g.n_cta * (int64_t)(P.g.row_bytes + P.g.srow_bytes) >= kDeepSingleBytes) {
-    const W4A8Plan D = plan_w4a8(shape, device, true, /*peer=*/true);
-    if (D.fast) {
-      P = D;
-      wide = true;
-    }
-  }
+  const bool wide = b.count > 1;
   for (int i0 = 0; i0 < b.count; i0 += kMaxItems) {
     const int n = std::min(kMaxItems, b.count - i0);
     GemvItems items{};
