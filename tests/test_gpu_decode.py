@@ -205,3 +205,56 @@ def test_layer_chain_bitwise_equals_single_layer_calls(ks, cuda, path, n_layers,
     assert status.cpu().tolist() == [0, 0]
     assert torch.isfinite(out).all() and out.abs().max() > 0
     np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), acts[n_layers].cpu().numpy().view(np.uint32))
+
+
+@pytest.mark.parametrize("ahead", ["0", "1", "6"])
+def test_chain_l2_lookahead_inert(cuda, ks, monkeypatch, ahead):
+    """The persistent kernel's L2 lookahead (slots prefetched while the ring
+    is full, KS_B200_DECODE_L2_AHEAD, default 3) only moves weights into L2
+    early: a four-layer chain gives bitwise the same output and intermediates
+    with any lookahead as with the default."""
+    import ctypes
+
+    import torch
+
+    monkeypatch.setenv("KS_B200_DECODE_PERSISTENT", "1")
+    L = ks.lib()
+    n = 4
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(901)
+    shapes = [(3 * H, H), (H, H), (I, H), (I, H), (H, I)]
+    W = [[torch.randint(0, 256, (r, c // 2), dtype=torch.uint8, device=cuda, generator=gen) for r, c in shapes]
+         for _ in range(n)]
+    S = [[(torch.rand((r, c // G), device=cuda, generator=gen) * 9e-3 + 1e-3).half() for r, c in shapes]
+         for _ in range(n)]
+    norms = torch.rand((n, 2, H), device=cuda, generator=gen) + 0.5
+    h0 = torch.rand(H, device=cuda, generator=gen) * 2 - 1
+    wl = (ctypes.c_void_p * (5 * n))(*[t.data_ptr() for Wl in W for t in Wl])
+    sl = (ctypes.c_void_p * (5 * n))(*[t.data_ptr() for Sl in S for t in Sl])
+    n1 = (ctypes.c_void_p * n)(*[norms[l, 0].data_ptr() for l in range(n)])
+    n2 = (ctypes.c_void_p * n)(*[norms[l, 1].data_ptr() for l in range(n)])
+    ws_bytes = L.ks_b200_decode_layers_workspace(H, I)
+    offs = (ctypes.c_size_t * 12)()
+    ks.check(L.ks_b200_decode_layer_offsets(H, I, offs))
+
+    def run(env):
+        if env is None:
+            monkeypatch.delenv("KS_B200_DECODE_L2_AHEAD", raising=False)
+        else:
+            monkeypatch.setenv("KS_B200_DECODE_L2_AHEAD", env)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=cuda)
+        out = torch.zeros(H, dtype=torch.float32, device=cuda)
+        status = torch.zeros(2, dtype=torch.int32, device=cuda)
+        torch.cuda.synchronize()
+        ks.check(L.ks_b200_decode_layers_w4a8_async(n, h0.data_ptr(), out.data_ptr(), n1, n2, EPS, wl, sl, H, I, G,
+                                                    ws.data_ptr(), ws_bytes, status.data_ptr(), None))
+        torch.cuda.synchronize()
+        assert status.cpu().tolist() == [0, 0]
+        w = ws.cpu().numpy()
+        w[offs[6] + 128:offs[6] + 256] = 0  # the grid-barrier counter advances every call
+        return out.cpu().numpy().view(np.uint32), w
+
+    y_def, w_def = run(None)
+    y, w = run(ahead)
+    np.testing.assert_array_equal(y, y_def)
+    np.testing.assert_array_equal(w, w_def)
